@@ -1,0 +1,168 @@
+// Native whole-forward runtime: y = final_norm(blocks(x)).
+//
+// Sequences, on the caller's stream, the same dataflow as the reference's
+// fused-norm CUDA path (torch_transformer_benchmark.py:1092-1148):
+//
+//   h   = LN(x; layers[0].norm1)                              [fp16]
+//   per layer l:
+//     qkv = h . Wqkv^T + bqkv                                 [fp16, tcgen05]
+//     ctx = attention(qkv)                                    [fp16]
+//     r   = ctx . Wo^T + bo + (l == 0 ? x : r)                [fp32, tcgen05]
+//     h   = LN(r; norm2)                                      [fp16]
+//     g   = gelu_erf(h . W1^T + b1)                           [fp16, tcgen05]
+//     r   = g . W2^T + b2 + r                                 [fp32, tcgen05]
+//     h   = LN(r; next norm1)  or  y = LN(r; final_norm)      [fp16 / fp32]
+//
+// The residual stream r stays fp32 end to end and the residual add happens
+// in the GEMM epilogue (in fp32, before any rounding), where the reference
+// adds an fp16-rounded update inside its LayerNorm kernel.
+// No allocation, no host synchronisation: graph-capturable.
+#include "internal.h"
+
+namespace tfx {
+namespace {
+
+__global__ void zero_padded_rows_kernel(float* y, int seq, int d, const int32_t* valid_len,
+                                        int64_t rows) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int b = static_cast<int>(row / seq), s = static_cast<int>(row % seq);
+  if (s < valid_len[b]) return;
+  float4* yr = reinterpret_cast<float4*>(y + row * d);
+  for (int c = threadIdx.x & 31; c < d / 4; c += 32) yr[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+constexpr size_t kAlign = 256;
+size_t round_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
+
+struct Workspace {
+  __half* h;
+  __half* qkv;
+  __half* ctx;
+  float* res;
+  __half* g;
+  size_t bytes;
+};
+
+Workspace plan_workspace(char* base, int64_t m, int d, int f) {
+  Workspace w{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    char* p = base ? base + off : nullptr;
+    off += round_up(bytes);
+    return p;
+  };
+  w.h = reinterpret_cast<__half*>(take(sizeof(__half) * m * d));
+  w.qkv = reinterpret_cast<__half*>(take(sizeof(__half) * m * 3 * d));
+  w.ctx = reinterpret_cast<__half*>(take(sizeof(__half) * m * d));
+  w.res = reinterpret_cast<float*>(take(sizeof(float) * m * d));
+  w.g = reinterpret_cast<__half*>(take(sizeof(__half) * m * f));
+  w.bytes = off;
+  return w;
+}
+
+int check_model(const tfx_model* mdl) {
+  if (mdl == nullptr || mdl->layers == nullptr)
+    return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward: null model");
+  const int d = mdl->d_model, h = mdl->num_heads, f = mdl->ffn_dim;
+  if (d <= 0 || h <= 0 || f <= 0 || mdl->num_layers <= 0)
+    return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward: model sizes must be positive");
+  if (d % h != 0) return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward: d_model %% num_heads != 0");
+  const int hd = d / h;
+  if (hd != 8 && hd != 16 && hd != 32 && hd != 64 && hd != 128 && hd != 256)
+    return fail(TFX_ERR_UNSUPPORTED, "tfx_forward: head_dim %d not in {8,16,32,64,128,256}", hd);
+  if (d % 32 != 0 || f % 32 != 0 || d > 4096)
+    return fail(TFX_ERR_UNSUPPORTED,
+                "tfx_forward: d_model and ffn_dim must be multiples of 32, d_model <= 4096");
+  for (int l = 0; l < mdl->num_layers; ++l) {
+    const tfx_layer& L = mdl->layers[l];
+    if (!L.norm1_weight || !L.norm1_bias || !L.qkv_weight || !L.qkv_bias || !L.out_weight ||
+        !L.out_bias || !L.norm2_weight || !L.norm2_bias || !L.ffn_in_weight || !L.ffn_in_bias ||
+        !L.ffn_out_weight || !L.ffn_out_bias)
+      return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward: layer %d has a null parameter", l);
+  }
+  if (!mdl->final_norm_weight || !mdl->final_norm_bias)
+    return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward: null final norm");
+  return TFX_OK;
+}
+
+}  // namespace
+}  // namespace tfx
+
+using namespace tfx;
+
+extern "C" {
+
+int64_t tfx_forward_workspace_bytes(const tfx_model* model, int batch, int seq) {
+  if (check_model(model) != TFX_OK || batch <= 0 || seq <= 0) return -1;
+  const int64_t m = static_cast<int64_t>(batch) * seq;
+  return static_cast<int64_t>(plan_workspace(nullptr, m, model->d_model, model->ffn_dim).bytes);
+}
+
+int tfx_forward(const tfx_model* model, const float* x, float* y, int batch, int seq,
+                const int32_t* valid_len, void* workspace, size_t workspace_bytes,
+                tfx_stream_t stream_) {
+  int st = check_model(model);
+  if (st != TFX_OK) return st;
+  if (x == nullptr || y == nullptr || workspace == nullptr)
+    return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward: null x, y or workspace");
+  if (batch <= 0 || seq <= 0)
+    return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward: batch and seq must be positive");
+  if (x == y) return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward: y must not alias x");
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(y) % 16 ||
+      reinterpret_cast<uintptr_t>(workspace) % kAlign)
+    return fail(TFX_ERR_MISALIGNED, "tfx_forward: x/y 16-byte and workspace 256-byte alignment");
+  const int64_t m = static_cast<int64_t>(batch) * seq;
+  const int d = model->d_model, f = model->ffn_dim, nh = model->num_heads, hd = d / nh;
+  const Workspace ws = plan_workspace(static_cast<char*>(workspace), m, d, f);
+  if (workspace_bytes < ws.bytes)
+    return fail(TFX_ERR_WORKSPACE, "tfx_forward: workspace %zu < required %zu bytes",
+                workspace_bytes, ws.bytes);
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  const float eps = model->eps;
+  const float scale = 1.0f / sqrtf(static_cast<float>(hd));
+
+  st = launch_layer_norm(x, model->layers[0].norm1_weight, model->layers[0].norm1_bias, ws.h,
+                         TFX_DTYPE_F16, m, d, eps, 1, stream);
+  if (st != TFX_OK) return st;
+  for (int l = 0; l < model->num_layers; ++l) {
+    const tfx_layer& L = model->layers[l];
+    const __half* wqkv = reinterpret_cast<const __half*>(L.qkv_weight);
+    st = launch_linear(ws.h, d, wqkv, L.qkv_bias, nullptr, 0, ws.qkv, 3 * d, m, 3 * d, d,
+                       TFX_EPI_BIAS, stream);
+    if (st != TFX_OK) return st;
+    st = launch_attention(ws.qkv, ws.qkv + d, ws.qkv + 2 * d, 3 * d, ws.ctx, d, batch, nh, seq,
+                          hd, scale, model->causal, valid_len, stream);
+    if (st != TFX_OK) return st;
+    st = launch_linear(ws.ctx, d, reinterpret_cast<const __half*>(L.out_weight), L.out_bias,
+                       l == 0 ? x : ws.res, d, ws.res, d, m, d, d, TFX_EPI_BIAS_RESIDUAL, stream);
+    if (st != TFX_OK) return st;
+    st = launch_layer_norm(ws.res, L.norm2_weight, L.norm2_bias, ws.h, TFX_DTYPE_F16, m, d, eps, 1,
+                           stream);
+    if (st != TFX_OK) return st;
+    st = launch_linear(ws.h, d, reinterpret_cast<const __half*>(L.ffn_in_weight), L.ffn_in_bias,
+                       nullptr, 0, ws.g, f, m, f, d, TFX_EPI_BIAS_GELU, stream);
+    if (st != TFX_OK) return st;
+    st = launch_linear(ws.g, f, reinterpret_cast<const __half*>(L.ffn_out_weight), L.ffn_out_bias,
+                       ws.res, d, ws.res, d, m, d, f, TFX_EPI_BIAS_RESIDUAL, stream);
+    if (st != TFX_OK) return st;
+    const bool last = l + 1 == model->num_layers;
+    if (!last) {
+      st = launch_layer_norm(ws.res, model->layers[l + 1].norm1_weight,
+                             model->layers[l + 1].norm1_bias, ws.h, TFX_DTYPE_F16, m, d, eps, 1,
+                             stream);
+    } else {
+      st = launch_layer_norm(ws.res, model->final_norm_weight, model->final_norm_bias, y,
+                             TFX_DTYPE_F32, m, d, eps, 1, stream);
+    }
+    if (st != TFX_OK) return st;
+  }
+  if (valid_len != nullptr) {
+    const int64_t blocks = (m + 7) / 8;
+    zero_padded_rows_kernel<<<blocks, 256, 0, stream>>>(y, seq, d, valid_len, m);
+    st = check_launch("zero_padded_rows_kernel");
+  }
+  return st;
+}
+
+}  // extern "C"

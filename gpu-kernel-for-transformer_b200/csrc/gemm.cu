@@ -1,0 +1,273 @@
+// Persistent, warp-specialised tcgen05 GEMM with fused epilogues.
+//
+//   out[m, n] = epi( sum_k A[m, k] * W[n, k] + bias[n] (, residual[m, n]) )
+//
+// A (activations) and W (nn.Linear weight, [out, in]) are fp16 and K-major,
+// so both feed tcgen05.mma directly from 128-byte-swizzled shared memory
+// written by TMA. The fp32 accumulator lives in TMEM, double-buffered so the
+// epilogue of tile i overlaps the MMAs of tile i+1.
+//
+// CTA = 6 warps, one CTA per SM, grid = min(#tiles, #SMs):
+//   warp 0      TMA producer (one lane): A and W k-blocks into a STAGES ring
+//   warp 1      TMEM allocator + MMA issuer (one lane)
+//   warps 2..5  epilogue: tcgen05.ld rows out of TMEM, bias / GELU / residual,
+//               store. Warp w may only touch TMEM lanes [32*(w%4), +32).
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace tfx {
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;  // 64 fp16 = one 128-byte swizzle row
+constexpr int kThreads = 192;
+
+template <int BN, int STAGES>
+struct GemmLayout {
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBarOffset = STAGES * kStageBytes;
+  static constexpr int kSmemBytes = kBarOffset + 256 + 1024;  // barriers + 1 KB alignment slack
+  static constexpr uint32_t kTmemCols = (2 * BN) < 32 ? 32 : (2 * BN);
+};
+
+template <int BN, int STAGES, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+                   const float* __restrict__ bias, const float* residual, void* out, int M, int N,
+                   int K, int64_t ldr, int64_t ldo, int* err) {
+  using L = GemmLayout<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int tiles_m = (M + kBM - 1) / kBM;
+  const int num_tiles = tiles_m * (N / BN);
+  const int kblocks = (K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmW);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, L::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------ TMA producer
+    int stage = 0;
+    uint32_t phase = 0;
+    int issued_parity[STAGES];
+    for (int s = 0; s < STAGES; ++s) issued_parity[s] = -1;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      const int m0 = (tile % tiles_m) * kBM;
+      const int n0 = (tile / tiles_m) * BN;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1, err, kDevTimeoutEmpty)) {
+          ok = false;
+          break;
+        }
+        uint8_t* sa = smem + stage * L::kStageBytes;
+        mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
+        tma_load_2d(sa, &tmA, &full[stage], kb * kBK, m0);
+        tma_load_2d(sa + L::kABytes, &tmW, &full[stage], kb * kBK, n0);
+        issued_parity[stage] = static_cast<int>(phase);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+    if (!ok) {
+      // Unwinding after a timeout: let our own copies land before exit.
+      for (int s = 0; s < STAGES; ++s)
+        if (issued_parity[s] >= 0) mbar_wait(&full[s], issued_parity[s], nullptr, 0);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // --------------------------------------------------------- MMA issuer
+    constexpr uint32_t idesc = idesc_f16_f32(kBM, BN);
+    int stage = 0;
+    uint32_t phase = 0;
+    int local = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+      const int buf = local & 1;
+      const uint32_t use = static_cast<uint32_t>(local >> 1);
+      if (!mbar_wait(&acc_empty[buf], (use & 1) ^ 1, err, kDevTimeoutAccumFree)) break;
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * BN);
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!mbar_wait(&full[stage], phase, err, kDevTimeoutFull)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(smem + stage * L::kStageBytes);
+        const uint32_t b_addr = a_addr + L::kABytes;
+#pragma unroll
+        for (int k = 0; k < kBK / 16; ++k) {
+          mma_f16_ss(d_tmem, sdesc_k_sw128(a_addr + k * 32), sdesc_k_sw128(b_addr + k * 32),
+                     idesc, (kb | k) != 0 ? 1u : 0u);
+        }
+        mma_commit(&empty[stage]);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (ok) mma_commit(&acc_full[buf]);
+    }
+  } else if (warp >= 2) {
+    // ----------------------------------------------------------- epilogue
+    const int quarter = warp & 3;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      const int buf = local & 1;
+      const uint32_t use = static_cast<uint32_t>(local >> 1);
+      if (!mbar_wait(&acc_full[buf], use & 1, err, kDevTimeoutAccum)) break;
+      tc_fence_after();
+      const int m0 = (tile % tiles_m) * kBM;
+      const int n0 = (tile / tiles_m) * BN;
+      const int row = m0 + quarter * 32 + lane;
+      const uint32_t t_row =
+          tmem_base + static_cast<uint32_t>(buf * BN) + (static_cast<uint32_t>(quarter * 32) << 16);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(t_row + c, r);
+        tmem_ld_wait();
+        float v[32];
+        const float4* b4 = reinterpret_cast<const float4*>(bias + n0 + c);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float4 bb = __ldg(b4 + j);
+          v[4 * j + 0] = __uint_as_float(r[4 * j + 0]) + bb.x;
+          v[4 * j + 1] = __uint_as_float(r[4 * j + 1]) + bb.y;
+          v[4 * j + 2] = __uint_as_float(r[4 * j + 2]) + bb.z;
+          v[4 * j + 3] = __uint_as_float(r[4 * j + 3]) + bb.w;
+        }
+        if (row < M) {
+          if constexpr (EPI == TFX_EPI_BIAS_RESIDUAL) {
+            const float4* res4 = reinterpret_cast<const float4*>(residual + row * ldr + n0 + c);
+            float4* o4 = reinterpret_cast<float4*>(static_cast<float*>(out) + row * ldo + n0 + c);
+            float4 rr[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) rr[j] = res4[j];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              o4[j] = make_float4(v[4 * j] + rr[j].x, v[4 * j + 1] + rr[j].y,
+                                  v[4 * j + 2] + rr[j].z, v[4 * j + 3] + rr[j].w);
+            }
+          } else {
+            if constexpr (EPI == TFX_EPI_BIAS_GELU) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
+            }
+            uint4* o4 = reinterpret_cast<uint4*>(static_cast<__half*>(out) + row * ldo + n0 + c);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              o4[j] = make_uint4(pack_half2(v[8 * j + 0], v[8 * j + 1]),
+                                 pack_half2(v[8 * j + 2], v[8 * j + 3]),
+                                 pack_half2(v[8 * j + 4], v[8 * j + 5]),
+                                 pack_half2(v[8 * j + 6], v[8 * j + 7]));
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, L::kTmemCols);
+}
+
+template <int BN, int STAGES, int EPI>
+int launch_gemm_t(const __half* a, int64_t lda, const __half* w, const float* bias,
+                  const float* residual, int64_t ldr, void* out, int64_t ldo, int64_t m, int n,
+                  int k, cudaStream_t stream) {
+  using L = GemmLayout<BN, STAGES>;
+  static int smem_done[kMaxDevices] = {0};
+  auto kern = gemm_tc_kernel<BN, STAGES, EPI>;
+  int st = ensure_smem(reinterpret_cast<const void*>(kern), L::kSmemBytes, smem_done);
+  if (st != TFX_OK) return st;
+  CUtensorMap tmA, tmW;
+  st = make_tmap_2d(&tmA, a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, static_cast<uint64_t>(m),
+                    static_cast<uint64_t>(k), static_cast<uint64_t>(lda), kBK, kBM,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != TFX_OK) return st;
+  st = make_tmap_2d(&tmW, w, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, static_cast<uint64_t>(n),
+                    static_cast<uint64_t>(k), static_cast<uint64_t>(k), kBK, BN,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != TFX_OK) return st;
+  const int64_t tiles = ((m + kBM - 1) / kBM) * (n / BN);
+  const int grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
+  kern<<<grid, kThreads, L::kSmemBytes, stream>>>(tmA, tmW, bias, residual, out,
+                                                   static_cast<int>(m), n, k, ldr, ldo,
+                                                   device_error_word());
+  return check_launch("gemm_tc_kernel");
+}
+
+template <int EPI>
+int launch_gemm_epi(const __half* a, int64_t lda, const __half* w, const float* bias,
+                    const float* residual, int64_t ldr, void* out, int64_t ldo, int64_t m, int n,
+                    int k, cudaStream_t stream) {
+  // Widest N tile that divides n: fewer, larger MMAs and fewer A re-reads.
+  if (n % 256 == 0 && n > 128)
+    return launch_gemm_t<256, 4, EPI>(a, lda, w, bias, residual, ldr, out, ldo, m, n, k, stream);
+  if (n % 128 == 0)
+    return launch_gemm_t<128, 6, EPI>(a, lda, w, bias, residual, ldr, out, ldo, m, n, k, stream);
+  if (n % 64 == 0)
+    return launch_gemm_t<64, 8, EPI>(a, lda, w, bias, residual, ldr, out, ldo, m, n, k, stream);
+  if (n % 32 == 0)
+    return launch_gemm_t<32, 8, EPI>(a, lda, w, bias, residual, ldr, out, ldo, m, n, k, stream);
+  return fail(TFX_ERR_UNSUPPORTED, "tfx_linear: n=%d must be a multiple of 32", n);
+}
+
+}  // namespace
+
+int launch_linear(const __half* a, int64_t lda, const __half* w, const float* bias,
+                  const float* residual, int64_t ldr, void* out, int64_t ldo, int64_t m, int n,
+                  int k, int epilogue, cudaStream_t stream) {
+  switch (epilogue) {
+    case TFX_EPI_BIAS:
+      return launch_gemm_epi<TFX_EPI_BIAS>(a, lda, w, bias, residual, ldr, out, ldo, m, n, k,
+                                           stream);
+    case TFX_EPI_BIAS_GELU:
+      return launch_gemm_epi<TFX_EPI_BIAS_GELU>(a, lda, w, bias, residual, ldr, out, ldo, m, n, k,
+                                                stream);
+    case TFX_EPI_BIAS_RESIDUAL:
+      return launch_gemm_epi<TFX_EPI_BIAS_RESIDUAL>(a, lda, w, bias, residual, ldr, out, ldo, m,
+                                                    n, k, stream);
+    default:
+      return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_linear: unknown epilogue %d", epilogue);
+  }
+}
+
+}  // namespace tfx

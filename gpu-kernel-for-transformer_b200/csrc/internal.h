@@ -1,0 +1,53 @@
+// Internal host-side declarations shared by the .cu translation units.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include "../../include/tfx.h"
+
+namespace tfx {
+
+// Records a human-readable detail for the calling thread and returns `status`.
+int fail(int status, const char* fmt, ...);
+
+// Checks cudaGetLastError after a launch; maps a failure to TFX_ERR_CUDA.
+int check_launch(const char* what);
+
+// Device error word (per device) the kernels write on a bounded-wait timeout.
+int* device_error_word();
+
+int num_sms();
+int current_device();
+
+// Opt a kernel into more than 48 KB of dynamic shared memory, once per device.
+int ensure_smem(const void* func, int bytes, int* done_flags /* [kMaxDevices] */);
+constexpr int kMaxDevices = 64;
+
+// cuTensorMapEncodeTiled resolved through the runtime (no -lcuda link).
+// 2-D fp16/fp32 row-major matrix [rows, cols] with row pitch `ld` elements;
+// box = box_cols x box_rows; swizzle as given.
+int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes,
+                 uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_cols, uint32_t box_rows,
+                 CUtensorMapSwizzle swizzle);
+
+// Kernel launchers (validated by the C-ABI layer before they are called).
+int launch_layer_norm(const float* x, const float* gamma, const float* beta, void* y, int y_dtype,
+                      int64_t rows, int d, float eps, int apply_affine, cudaStream_t stream);
+int launch_residual_layer_norm(const float* r, const __half* u, const float* gamma,
+                               const float* beta, float* r_out, void* y, int y_dtype,
+                               int64_t rows, int d, float eps, int apply_affine,
+                               cudaStream_t stream);
+int launch_linear(const __half* a, int64_t lda, const __half* w, const float* bias,
+                  const float* residual, int64_t ldr, void* out, int64_t ldo, int64_t m, int n,
+                  int k, int epilogue, cudaStream_t stream);
+int launch_attention(const __half* q, const __half* k, const __half* v, int64_t ld_qkv,
+                     __half* out, int64_t ld_out, int batch, int heads, int seq, int head_dim,
+                     float scale, int causal, const int32_t* valid_len, cudaStream_t stream);
+
+}  // namespace tfx

@@ -1,0 +1,383 @@
+"""Drop-in module API: ``TransformerConfig``, ``BaselineTransformer`` and
+``UserOptimizedTransformer`` with the reference's constructor, parameter
+names/layout, toggles and ``forward(x, valid_token_mask)`` contract
+(torch_transformer_benchmark.py:47-74, 204-317, 320-1148).
+
+``UserOptimizedTransformer.forward`` makes ONE call into the native runtime
+(``tfx_forward`` in lib/libtfx_b200.so), which enqueues every kernel of the
+forward on the current stream. Nothing here computes on the CPU: a CPU input
+raises (the reference's CPU fallback, torch_transformer_benchmark.py:1003-1006,
+is deliberately not reproduced), as does a missing library.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import warnings
+from dataclasses import dataclass
+from typing import Dict, Optional, Tuple
+
+import torch
+import torch.nn as nn
+
+from . import _lib
+
+
+@dataclass(frozen=True)
+class TransformerConfig:
+    """torch_transformer_benchmark.py:47-74 (same fields, same validation)."""
+
+    batch_size: int
+    seq_len: int
+    d_model: int
+    num_heads: int
+    ffn_dim: int
+    num_layers: int
+    causal: bool
+
+    def validate(self) -> None:
+        if self.batch_size <= 0:
+            raise ValueError("batch_size must be positive")
+        if self.seq_len <= 0:
+            raise ValueError("seq_len must be positive")
+        if self.d_model <= 0:
+            raise ValueError("d_model must be positive")
+        if self.num_heads <= 0:
+            raise ValueError("num_heads must be positive")
+        if self.d_model % self.num_heads != 0:
+            raise ValueError(
+                f"d_model ({self.d_model}) must be divisible by "
+                f"num_heads ({self.num_heads})"
+            )
+        if self.ffn_dim <= 0:
+            raise ValueError("ffn_dim must be positive")
+        if self.num_layers <= 0:
+            raise ValueError("num_layers must be positive")
+
+
+# The reference's official shape table (torch_transformer_benchmark.py:80-95);
+# ids 3, 6, 8, 11 and 14 are the benchmark configs c1..c5.
+OFFICIAL_BENCHMARK_SHAPES: Dict[int, TransformerConfig] = {
+    1: TransformerConfig(64, 128, 128, 4, 128, 4, True),
+    2: TransformerConfig(1, 128, 128, 4, 128, 4, True),
+    3: TransformerConfig(4, 128, 128, 4, 128, 4, True),
+    4: TransformerConfig(16, 128, 128, 4, 128, 4, True),
+    5: TransformerConfig(128, 128, 128, 4, 128, 4, True),
+    6: TransformerConfig(10000, 128, 128, 4, 128, 4, True),
+    7: TransformerConfig(64, 128, 32, 4, 32, 4, True),
+    8: TransformerConfig(64, 128, 1024, 4, 1024, 4, True),
+    9: TransformerConfig(64, 128, 128, 1, 128, 4, True),
+    10: TransformerConfig(64, 128, 128, 2, 128, 4, True),
+    11: TransformerConfig(64, 128, 128, 16, 128, 4, True),
+    12: TransformerConfig(64, 32, 128, 4, 128, 4, True),
+    13: TransformerConfig(64, 1024, 128, 4, 128, 4, True),
+    14: TransformerConfig(32, 100000, 1024, 16, 1024, 2, True),
+}
+
+
+class _SelfAttentionParams(nn.Module):
+    """Parameter container with BaselineSelfAttention's names and creation
+    order (torch_transformer_benchmark.py:207-220)."""
+
+    def __init__(self, d_model: int, num_heads: int) -> None:
+        super().__init__()
+        if d_model % num_heads != 0:
+            raise ValueError("d_model must be divisible by num_heads")
+        self.d_model = d_model
+        self.num_heads = num_heads
+        self.head_dim = d_model // num_heads
+        self.scale = self.head_dim ** -0.5
+        self.q_proj = nn.Linear(d_model, d_model, bias=True)
+        self.k_proj = nn.Linear(d_model, d_model, bias=True)
+        self.v_proj = nn.Linear(d_model, d_model, bias=True)
+        self.out_proj = nn.Linear(d_model, d_model, bias=True)
+
+
+class _BlockParams(nn.Module):
+    """BaselineTransformerBlock's parameters (torch_transformer_benchmark.py:270-277)."""
+
+    def __init__(self, d_model: int, num_heads: int, ffn_dim: int) -> None:
+        super().__init__()
+        self.norm1 = nn.LayerNorm(d_model)
+        self.attention = _SelfAttentionParams(d_model, num_heads)
+        self.norm2 = nn.LayerNorm(d_model)
+        self.ffn_in = nn.Linear(d_model, ffn_dim)
+        self.ffn_out = nn.Linear(ffn_dim, d_model)
+
+
+class BaselineTransformer(nn.Module):
+    """The reference model's module tree (torch_transformer_benchmark.py:293-305).
+
+    Constructing it under ``torch.manual_seed(s)`` draws exactly the weights
+    the reference draws, and its state_dict keys are the reference's, so
+    ``load_state_dict`` of a reference checkpoint works unchanged. This
+    package ships only the B200 path: the explicit FP32 eager forward is the
+    reference's own code and is not duplicated here.
+    """
+
+    def __init__(self, config: TransformerConfig) -> None:
+        super().__init__()
+        self.config = config
+        self.layers = nn.ModuleList(
+            [
+                _BlockParams(config.d_model, config.num_heads, config.ffn_dim)
+                for _ in range(config.num_layers)
+            ]
+        )
+        self.final_norm = nn.LayerNorm(config.d_model)
+
+    def forward(self, x, valid_token_mask=None):  # pragma: no cover - documented stub
+        raise NotImplementedError(
+            "this package provides only the CUDA path (UserOptimizedTransformer); the "
+            "explicit FP32 baseline forward is the reference implementation's"
+        )
+
+
+@dataclass(frozen=True)
+class ShapeExecutionPlan:
+    """Diagnostic description of the kernels a config runs
+    (the reference's per-shape plan, torch_transformer_benchmark.py:98-157)."""
+
+    official_shape_id: Optional[int]
+    head_dim: int
+    gemm_tiles: str
+    attention: str
+
+    def describe(self) -> str:
+        shape = (
+            f"official-{self.official_shape_id}"
+            if self.official_shape_id is not None
+            else "general"
+        )
+        return (
+            f"{shape}: gemm=tcgen05 {self.gemm_tiles}, attention={self.attention} "
+            f"(head_dim {self.head_dim}), norm=fused fp32 LayerNorm"
+        )
+
+
+def _plan_for(config: TransformerConfig) -> ShapeExecutionPlan:
+    ids = {c: i for i, c in OFFICIAL_BENCHMARK_SHAPES.items()}
+    hd = config.d_model // config.num_heads
+    widest = max(t for t in (256, 128, 64, 32) if config.d_model % t == 0) if \
+        config.d_model % 32 == 0 else 0
+    return ShapeExecutionPlan(
+        official_shape_id=ids.get(config),
+        head_dim=hd,
+        gemm_tiles=f"128x{min(widest, 256)} persistent",
+        attention="flash (online softmax, streamed K/V)",
+    )
+
+
+def _version(t: torch.Tensor) -> Optional[int]:
+    try:
+        return t._version
+    except RuntimeError:  # inference tensors expose no version counter
+        return None
+
+
+class UserOptimizedTransformer(BaselineTransformer):
+    """B200 inference module; same API as the reference's
+    (torch_transformer_benchmark.py:320-1148)."""
+
+    def __init__(self, config: TransformerConfig) -> None:
+        super().__init__(config)
+        self._shape_execution_plan = _plan_for(config)
+        self._mixed_precision_dtype: Optional[torch.dtype] = torch.float16
+        self._kv_cache_enabled = False
+        self._packed = None  # (key, tensors, ctypes structs)
+        self._workspace: Dict[torch.device, torch.Tensor] = {}
+        self._mask_cache = None
+
+    # ------------------------------------------------------------ toggles
+    @property
+    def shape_execution_plan(self) -> ShapeExecutionPlan:
+        return self._shape_execution_plan
+
+    def enable_mixed_precision(self, dtype: Optional[torch.dtype] = torch.float16) -> None:
+        """torch_transformer_benchmark.py:369-377. Tensor-core operands are
+        always fp16: bf16 fails the accuracy rule on these configs, so a bf16
+        request is accepted with a warning and runs fp16; None (pure FP32 GPU
+        compute) is not provided by this implementation."""
+        if dtype not in (None, torch.float16, torch.bfloat16):
+            raise ValueError("mixed precision dtype must be float16 or bfloat16")
+        if dtype is None:
+            raise NotImplementedError(
+                "the B200 path computes tensor-core operands in fp16; there is no FP32 path"
+            )
+        if dtype == torch.bfloat16:
+            warnings.warn("bfloat16 operands exceed the accuracy tolerance; using float16")
+        self._mixed_precision_dtype = torch.float16
+
+    def enable_triton_fused_norm(self, enabled: bool = True) -> None:
+        """Kept for API compatibility: normalisation is always the fused
+        native kernel (there is no unfused fallback)."""
+        if not enabled:
+            raise NotImplementedError("the native path has no unfused LayerNorm fallback")
+
+    def enable_triton_fused_ffn(self, enabled: bool = True) -> None:
+        """Kept for API compatibility: the FFN always runs the native
+        tcgen05 GEMM with the fused GELU epilogue."""
+        if not enabled:
+            raise NotImplementedError("the native path has no unfused FFN fallback")
+
+    def enable_attention_fp16_accumulation(self, enabled: bool = True) -> None:
+        """torch_transformer_benchmark.py:395-407: fp16 accumulation is never
+        used (every accumulator is fp32), so only False is meaningful."""
+        if enabled and self.config.causal:
+            raise ValueError(
+                "FP16 attention accumulation is disabled for causal models "
+                "because it exceeds the accuracy tolerance"
+            )
+
+    def enable_kv_cache(self, enabled: bool = True) -> None:
+        """Incremental decoding (torch_transformer_benchmark.py:409-462) is not
+        part of this build's forward path."""
+        if enabled:
+            raise NotImplementedError("KV-cache decoding is not implemented in the B200 path")
+        self._kv_cache_enabled = False
+
+    def reset_kv_cache(self) -> None:
+        pass
+
+    @property
+    def kv_cache_length(self) -> int:
+        return 0
+
+    # ---------------------------------------------------------- packing
+    def _param_key(self, device: torch.device) -> Tuple:
+        key = [device]
+        for p in self.parameters():
+            key.append((p.data_ptr(), _version(p), p.dtype))
+        return tuple(key)
+
+    def _prepare(self, device: torch.device):
+        """Pack the weights once per parameter version (the reference's
+        version-checked caches, torch_transformer_benchmark.py:524-655):
+        fp16 [out, in] GEMM weights (q|k|v stacked), fp32 biases and norms."""
+        key = self._param_key(device)
+        if self._packed is not None and self._packed[0] == key and \
+                all(k[1] is not None for k in key[1:]):
+            return self._packed
+        keep = []
+
+        def f32(t):
+            t = t.detach().to(device=device, dtype=torch.float32).contiguous()
+            keep.append(t)
+            return t.data_ptr()
+
+        def f16(t):
+            t = t.detach().to(device=device, dtype=torch.float16).contiguous()
+            keep.append(t)
+            return t.data_ptr()
+
+        layers = (_lib.TfxLayer * self.config.num_layers)()
+        for i, blk in enumerate(self.layers):
+            att = blk.attention
+            L = layers[i]
+            L.norm1_weight = f32(blk.norm1.weight)
+            L.norm1_bias = f32(blk.norm1.bias)
+            L.qkv_weight = f16(torch.cat(
+                (att.q_proj.weight, att.k_proj.weight, att.v_proj.weight), dim=0))
+            L.qkv_bias = f32(torch.cat((att.q_proj.bias, att.k_proj.bias, att.v_proj.bias)))
+            L.out_weight = f16(att.out_proj.weight)
+            L.out_bias = f32(att.out_proj.bias)
+            L.norm2_weight = f32(blk.norm2.weight)
+            L.norm2_bias = f32(blk.norm2.bias)
+            L.ffn_in_weight = f16(blk.ffn_in.weight)
+            L.ffn_in_bias = f32(blk.ffn_in.bias)
+            L.ffn_out_weight = f16(blk.ffn_out.weight)
+            L.ffn_out_bias = f32(blk.ffn_out.bias)
+        model = _lib.TfxModel()
+        model.d_model = self.config.d_model
+        model.num_heads = self.config.num_heads
+        model.ffn_dim = self.config.ffn_dim
+        model.num_layers = self.config.num_layers
+        model.causal = int(self.config.causal)
+        model.eps = float(self.final_norm.eps)
+        model.layers = ctypes.cast(layers, ctypes.POINTER(_lib.TfxLayer))
+        model.final_norm_weight = f32(self.final_norm.weight)
+        model.final_norm_bias = f32(self.final_norm.bias)
+        self._packed = (key, keep, layers, model)
+        return self._packed
+
+    def _workspace_for(self, device: torch.device, model, batch: int, seq: int) -> torch.Tensor:
+        need = _lib.load().tfx_forward_workspace_bytes(ctypes.byref(model), batch, seq)
+        if need < 0:
+            _lib.check(_lib.TFX_ERR_INVALID_ARGUMENT, "tfx_forward_workspace_bytes")
+        ws = self._workspace.get(device)
+        if ws is None or ws.numel() < need:
+            ws = torch.empty(int(need), dtype=torch.uint8, device=device)
+            self._workspace[device] = ws
+        return ws
+
+    # ------------------------------------------------------------- masks
+    def _valid_lengths(self, x: torch.Tensor, mask: Optional[torch.Tensor]):
+        """All-True (or None) -> None; prefix-valid mask -> int32 lengths.
+
+        Inspected once per mask object and version, like the reference's
+        cached mask preparation (torch_transformer_benchmark.py:464-522),
+        so graph capture sees no host synchronisation.
+        """
+        if mask is None:
+            return None
+        if mask.shape != x.shape[:2] or mask.dtype != torch.bool:
+            raise ValueError("valid_token_mask must be a [B, S] bool tensor")
+        ver = _version(mask)
+        c = self._mask_cache
+        if c is not None and ver is not None and c[0] is mask and c[1] == ver:
+            return c[2]
+        m = mask.to(x.device)
+        if bool(m.all().item()):
+            result = None
+        else:
+            lengths = m.sum(dim=1, dtype=torch.int32)
+            prefix = torch.arange(m.shape[1], device=m.device)[None, :] < lengths[:, None]
+            if not bool(torch.equal(prefix, m)):
+                raise NotImplementedError(
+                    "only prefix-valid padding masks (the reference's generator form) are "
+                    "supported"
+                )
+            result = lengths.contiguous()
+        if ver is not None:
+            self._mask_cache = (mask, ver, result)
+        return result
+
+    # ----------------------------------------------------------- forward
+    def forward(
+        self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None
+    ) -> torch.Tensor:
+        if x.device.type != "cuda":
+            raise RuntimeError(
+                "UserOptimizedTransformer runs only on CUDA (sm_100a); there is no CPU fallback"
+            )
+        if x.dim() != 3 or x.shape[-1] != self.config.d_model:
+            raise ValueError(f"expected x of shape [B, S, {self.config.d_model}]")
+        if x.dtype != torch.float32:
+            raise ValueError("x must be float32 (the residual stream is fp32)")
+        x = x.contiguous()
+        batch, seq, _ = x.shape
+        valid_len = self._valid_lengths(x, valid_token_mask)
+        _, _, _, model = self._prepare(x.device)
+        ws = self._workspace_for(x.device, model, batch, seq)
+        y = torch.empty_like(x)
+        self.run_into(x, y, valid_len, ws)
+        return y
+
+    def run_into(self, x: torch.Tensor, y: torch.Tensor,
+                 valid_len: Optional[torch.Tensor] = None,
+                 workspace: Optional[torch.Tensor] = None) -> None:
+        """Enqueue the forward of ``x`` into the preallocated ``y`` (no
+        allocation when ``workspace`` is given: safe inside graph capture)."""
+        _, _, _, model = self._prepare(x.device)
+        batch, seq, _ = x.shape
+        if workspace is None:
+            workspace = self._workspace_for(x.device, model, batch, seq)
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+        _lib.check(
+            _lib.load().tfx_forward(
+                ctypes.byref(model), x.data_ptr(), y.data_ptr(), batch, seq,
+                valid_len.data_ptr() if valid_len is not None else None,
+                workspace.data_ptr(), workspace.numel(), stream,
+            ),
+            "tfx_forward",
+        )

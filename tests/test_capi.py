@@ -1,0 +1,105 @@
+"""The C-ABI library: it loads without a GPU, exports every symbol that
+include/tfx.h declares, and rejects bad arguments on the host (no kernel is
+launched, no CUDA call made) with the documented status codes."""
+
+from __future__ import annotations
+
+import ctypes
+import pathlib
+import re
+
+import pytest
+
+from conftest import ROOT, load_package
+
+HEADER = ROOT / "include" / "tfx.h"
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?[\w\s\*]+?\b(tfx_\w+)\s*\(", text, re.M)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    pkg = load_package()
+    build = __import__("importlib").import_module(pkg.__name__ + ".build")
+    build.build()
+    return pkg._lib.load()
+
+
+def test_header_declares_the_expected_api():
+    syms = declared_symbols()
+    for name in ("tfx_layer_norm", "tfx_residual_layer_norm", "tfx_linear", "tfx_attention",
+                 "tfx_forward", "tfx_forward_workspace_bytes", "tfx_version"):
+        assert name in syms
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+
+
+def test_python_binding_covers_the_header():
+    pkg = load_package()
+    assert set(declared_symbols()) == set(pkg._lib.SIGNATURES)
+
+
+def test_version_and_status_strings(lib):
+    assert lib.tfx_version() >= 100
+    assert lib.tfx_status_string(0) == b"ok"
+    assert b"alignment" in lib.tfx_status_string(-3) or b"misaligned" in lib.tfx_status_string(-3)
+
+
+def test_host_side_argument_errors(lib):
+    pkg = load_package()
+    L = pkg._lib
+    # null tensors
+    assert lib.tfx_linear(None, None, None, None, None, 4, 32, 8, 0, None) == L.TFX_ERR_INVALID_ARGUMENT
+    assert b"null" in lib.tfx_last_error_message()
+    # unsupported shapes are rejected before any device work
+    fake = ctypes.c_void_p(256)
+    assert lib.tfx_linear(fake, fake, fake, None, fake, 4, 33, 8, 0, None) == L.TFX_ERR_UNSUPPORTED
+    assert lib.tfx_linear(fake, fake, fake, None, fake, 4, 32, 8, 2, None) == L.TFX_ERR_INVALID_ARGUMENT
+    assert lib.tfx_linear(fake, fake, fake, None, fake, 4, 32, 8, 9, None) in (
+        L.TFX_ERR_INVALID_ARGUMENT,)
+    odd = ctypes.c_void_p(258)
+    assert lib.tfx_linear(odd, fake, fake, None, fake, 4, 32, 8, 0, None) == L.TFX_ERR_MISALIGNED
+    assert lib.tfx_layer_norm(fake, fake, fake, fake, 0, 4, 30, 1e-5, 1, None) == L.TFX_ERR_UNSUPPORTED
+    assert lib.tfx_layer_norm(fake, fake, fake, fake, 7, 4, 32, 1e-5, 1, None) == L.TFX_ERR_INVALID_ARGUMENT
+    assert lib.tfx_attention(fake, fake, fake, 96, fake, 96, 1, 4, 16, 24, 0.2, 1, None, None) == \
+        L.TFX_ERR_UNSUPPORTED
+    assert lib.tfx_attention(fake, fake, fake, 64, fake, 96, 1, 4, 16, 24, 0.2, 1, None, None) == \
+        L.TFX_ERR_INVALID_ARGUMENT
+
+
+def test_forward_rejects_bad_models(lib):
+    pkg = load_package()
+    L = pkg._lib
+    m = L.TfxModel()
+    m.d_model, m.num_heads, m.ffn_dim, m.num_layers = 128, 5, 128, 1
+    assert lib.tfx_forward_workspace_bytes(ctypes.byref(m), 1, 1) == -1
+    layers = (L.TfxLayer * 1)()
+    m.layers = ctypes.cast(layers, ctypes.POINTER(L.TfxLayer))
+    m.num_heads = 4
+    # every pointer null -> invalid argument, nothing launched
+    assert lib.tfx_forward(ctypes.byref(m), ctypes.c_void_p(256), ctypes.c_void_p(512), 1, 1,
+                           None, ctypes.c_void_p(1024), 1 << 20, None) == L.TFX_ERR_INVALID_ARGUMENT
+    m.num_heads = 3  # head_dim not integral
+    assert lib.tfx_forward_workspace_bytes(ctypes.byref(m), 1, 1) == -1
+
+
+def test_workspace_size_formula(lib):
+    pkg = load_package()
+    L = pkg._lib
+    m = L.TfxModel()
+    m.d_model, m.num_heads, m.ffn_dim, m.num_layers = 128, 4, 128, 1
+    layers = (L.TfxLayer * 1)()
+    for f, _ in L.TfxLayer._fields_:
+        setattr(layers[0], f, 256)
+    m.layers = ctypes.cast(layers, ctypes.POINTER(L.TfxLayer))
+    m.final_norm_weight = m.final_norm_bias = 256
+    rows = 10 * 128
+    need = lib.tfx_forward_workspace_bytes(ctypes.byref(m), 10, 128)
+    # h, qkv, ctx (fp16, D, 3D, D) + residual (fp32, D) + ffn hidden (fp16, F)
+    assert need == rows * (2 * 128 + 2 * 384 + 2 * 128 + 4 * 128 + 2 * 128)

@@ -1,0 +1,176 @@
+"""Per-kernel parity on a B200, through the C ABI (ctypes -> libtfx_b200.so).
+
+Each kernel is compared with an fp32/fp64 CPU computation on the same
+(fp16-rounded, where the kernel consumes fp16) inputs:
+
+* LayerNorm / residual LayerNorm: fp32 statistics, fp16 or fp32 output;
+  tolerance = one fp16 ulp of the output (rtol 2**-10) + 1e-5 absolute.
+* Tensor-core linear: fp32 accumulation of fp16 products; tolerance
+  rtol 2e-3 + atol 2e-3 on fp16 outputs, 1e-4 on fp32 (residual) outputs.
+* Attention: fp64 softmax reference on the fp16 q/k/v; the kernel rounds P
+  to fp16 before P.V, so tolerance atol 2e-3.
+"""
+
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda:0")
+
+
+def _randn(*shape, seed=0, scale=1.0):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(*shape, generator=g) * scale
+
+
+@pytest.mark.parametrize("rows,d", [(1, 128), (777, 128), (513, 1024), (64, 96), (33, 4096)])
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32])
+def test_layer_norm(pkg, dev, rows, d, out_dtype):
+    x = _randn(rows, d, seed=rows + d) * 3 + 0.5
+    w = _randn(d, seed=1) * 0.2 + 1
+    b = _randn(d, seed=2) * 0.1
+    ref = torch.nn.functional.layer_norm(x, (d,), w, b, 1e-5)
+    got = pkg.ops.layer_norm(x.to(dev), w.to(dev), b.to(dev), 1e-5, out_dtype).float().cpu()
+    tol = 2 ** -10 if out_dtype == torch.float16 else 1e-6
+    assert torch.allclose(got, ref, rtol=tol, atol=1e-5 + tol), (got - ref).abs().max()
+
+
+@pytest.mark.parametrize("rows,d", [(300, 128), (100, 1024)])
+@pytest.mark.parametrize("store", [True, False])
+def test_residual_layer_norm(pkg, dev, rows, d, store):
+    r = _randn(rows, d, seed=3)
+    u = _randn(rows, d, seed=4).half()
+    w = torch.ones(d)
+    b = torch.zeros(d)
+    s = r + u.float()
+    ref = torch.nn.functional.layer_norm(s, (d,), w, b, 1e-5)
+    r_out, n = pkg.ops.fused_residual_layer_norm(
+        r.to(dev), u.to(dev), w.to(dev), b.to(dev), 1e-5, torch.float16, store_residual=store
+    )
+    assert torch.allclose(n.float().cpu(), ref, rtol=2 ** -10, atol=2e-3)
+    if store:
+        assert torch.allclose(r_out.cpu(), s, atol=1e-6)
+
+
+GEMM_SHAPES = [
+    # (m, n, k): c1/c2/c4 projections, c3/c5 projections, ragged edges
+    (512, 384, 128),
+    (512, 128, 128),
+    (1000, 128, 128),
+    (8192, 3072, 1024),
+    (1200, 1024, 1024),
+    (130, 256, 1024),
+    (77, 96, 40),
+    (1, 32, 8),
+    (40000, 128, 128),
+]
+
+
+@pytest.mark.parametrize("m,n,k", GEMM_SHAPES)
+@pytest.mark.parametrize("epi", ["bias", "gelu", "residual"])
+def test_linear(pkg, dev, m, n, k, epi):
+    a = _randn(m, k, seed=m + k).half()
+    w = (_randn(n, k, seed=n + 7) / math.sqrt(k)).half()
+    bias = _randn(n, seed=5) * 0.1
+    acc = a.float() @ w.float().T + bias
+    if epi == "bias":
+        got = pkg.ops.linear(a.to(dev), w.to(dev), bias.to(dev)).float().cpu()
+        ref = acc
+        tol = 2e-3
+    elif epi == "gelu":
+        got = pkg.ops.linear_gelu(a.to(dev), w.to(dev), bias.to(dev)).float().cpu()
+        ref = torch.nn.functional.gelu(acc, approximate="none")
+        tol = 2e-3
+    else:
+        res = _randn(m, n, seed=9)
+        got = pkg.ops.linear_residual(a.to(dev), w.to(dev), bias.to(dev), res.to(dev)).cpu()
+        ref = acc + res
+        tol = 1e-4
+    err = (got - ref).abs()
+    bound = tol + tol * ref.abs()
+    assert bool((err <= bound).all()), f"max err {err.max():.3g} at {int(err.argmax())}"
+
+
+def _attn_ref(q, k, v, causal, valid_len=None):
+    """fp64 softmax(QK^T/sqrt(hd)) V on [B, S, H, hd] fp16 inputs."""
+    b, s, h, hd = q.shape
+    qd, kd, vd = (t.double().permute(0, 2, 1, 3) for t in (q, k, v))
+    sc = (qd @ kd.transpose(-1, -2)) / math.sqrt(hd)
+    if causal:
+        sc = sc.masked_fill(torch.ones(s, s, dtype=torch.bool).triu(1), float("-inf"))
+    if valid_len is not None:
+        keymask = torch.arange(s)[None, :] >= valid_len[:, None]
+        sc = sc.masked_fill(keymask[:, None, None, :], float("-inf"))
+    p = torch.softmax(sc, dim=-1)
+    p = torch.nan_to_num(p, nan=0.0)
+    return (p @ vd).permute(0, 2, 1, 3).reshape(b, s, h * hd)
+
+
+ATTN_CASES = [
+    # (batch, seq, heads, hd, causal)
+    (2, 128, 4, 32, True),
+    (2, 128, 16, 8, True),
+    (1, 128, 4, 256, True),
+    (1, 300, 16, 64, True),
+    (3, 37, 4, 32, True),
+    (2, 1, 4, 32, True),
+    (1, 200, 2, 128, True),
+    (2, 70, 8, 16, True),
+    (2, 100, 4, 32, False),
+    (1, 64, 2, 256, False),
+]
+
+
+@pytest.mark.parametrize("b,s,h,hd,causal", ATTN_CASES)
+def test_attention(pkg, dev, b, s, h, hd, causal):
+    qkv = _randn(b, s, 3, h, hd, seed=b * 1000 + s + hd).half()
+    q, k, v = qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2]
+    ref = _attn_ref(q, k, v, causal)
+    g = qkv.to(dev)
+    got = pkg.ops.attention(g[:, :, 0], g[:, :, 1], g[:, :, 2], is_causal=causal)
+    err = (got.double().cpu() - ref).abs().max().item()
+    assert err < 2e-3, err
+
+
+def test_attention_key_padding(pkg, dev):
+    b, s, h, hd = 3, 128, 4, 32
+    qkv = _randn(b, s, 3, h, hd, seed=11).half()
+    lengths = torch.tensor([128, 97, 5], dtype=torch.int32)
+    ref = _attn_ref(qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2], True, lengths)
+    g = qkv.to(dev)
+    got = pkg.ops.attention(g[:, :, 0], g[:, :, 1], g[:, :, 2], is_causal=True,
+                            valid_lengths=lengths.to(dev))
+    err = (got.double().cpu() - ref).abs().max().item()
+    assert err < 2e-3, err
+
+
+def test_attention_long_sequence_rows(pkg, dev):
+    """A long causal sequence (S=4096, hd=64): spot-check late query rows
+    against the blockwise fp64 oracle."""
+    from oracle.baseline import blockwise_causal_attention_fp64
+
+    s, h, hd = 4096, 2, 64
+    qkv = _randn(1, s, 3, h, hd, seed=21).half()
+    g = qkv.to(dev)
+    got = pkg.ops.attention(g[:, :, 0], g[:, :, 1], g[:, :, 2], is_causal=True).cpu()
+    for head in range(h):
+        ref = blockwise_causal_attention_fp64(
+            qkv[0, :, 0, head], qkv[0, :, 1, head], qkv[0, :, 2, head], hd ** -0.5
+        )
+        err = (got[0, :, head * hd:(head + 1) * hd].double() - ref).abs().max().item()
+        assert err < 2e-3, (head, err)
+
+
+def test_no_device_timeout_recorded(pkg, dev):
+    torch.cuda.synchronize()
+    assert pkg._lib.read_device_error() == 0

@@ -1,0 +1,126 @@
+"""Host-side logic of the drop-in module, on the CPU (no GPU, no kernels):
+config validation, parameter names and seeded initialisation identical to
+the reference model, weight packing layout, mask handling, and the
+no-fallback rule."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from conftest import load_golden
+from oracle import baseline as ob
+
+
+def test_config_validation_matches_reference(pkg):
+    pkg.TransformerConfig(4, 128, 128, 4, 128, 4, True).validate()
+    bad = [
+        dict(batch_size=0), dict(seq_len=0), dict(d_model=0), dict(num_heads=0),
+        dict(num_heads=3), dict(ffn_dim=0), dict(num_layers=0),
+    ]
+    base = dict(batch_size=4, seq_len=128, d_model=128, num_heads=4, ffn_dim=128,
+                num_layers=4, causal=True)
+    for b in bad:
+        kw = {**base, **b}
+        with pytest.raises(ValueError):
+            pkg.TransformerConfig(**kw).validate()
+        with pytest.raises(ValueError):
+            ob.TransformerConfig(**kw).validate()
+
+
+def test_official_shapes_contain_the_benchmark_configs(pkg):
+    shapes = pkg.OFFICIAL_BENCHMARK_SHAPES
+    assert shapes[3] == pkg.TransformerConfig(4, 128, 128, 4, 128, 4, True)
+    assert shapes[6] == pkg.TransformerConfig(10000, 128, 128, 4, 128, 4, True)
+    assert shapes[8] == pkg.TransformerConfig(64, 128, 1024, 4, 1024, 4, True)
+    assert shapes[11] == pkg.TransformerConfig(64, 128, 128, 16, 128, 4, True)
+    assert shapes[14] == pkg.TransformerConfig(32, 100000, 1024, 16, 1024, 2, True)
+    assert "official-6" in pkg.UserOptimizedTransformer(shapes[6]).shape_execution_plan.describe()
+
+
+@pytest.mark.parametrize("name", ["c1", "c3_b1", "c5_s256"])
+def test_seeded_init_and_state_dict_match_reference(pkg, name):
+    """torch.manual_seed(s) + construction draws the reference's weights, and
+    the state_dict keys are the reference's (golden state hash)."""
+    rec = load_golden(name)
+    torch.manual_seed(rec["model_seed"])
+    cand = pkg.UserOptimizedTransformer(pkg.TransformerConfig(**rec["config"]))
+    assert ob.state_dict_checksum(cand) == rec["state_sha256"]
+    oracle_model = ob.make_baseline(ob.TransformerConfig(**rec["config"]), rec["model_seed"])
+    assert list(cand.state_dict().keys()) == list(oracle_model.state_dict().keys())
+    cand.load_state_dict(oracle_model.state_dict(), strict=True)
+
+
+def test_weight_packing_layout(pkg):
+    cfg = pkg.TransformerConfig(2, 16, 64, 4, 96, 2, True)
+    torch.manual_seed(0)
+    m = pkg.UserOptimizedTransformer(cfg)
+    key, keep, layers, model = m._prepare(torch.device("cpu"))
+    assert model.d_model == 64 and model.num_heads == 4 and model.ffn_dim == 96
+    assert model.num_layers == 2 and model.causal == 1
+    ptrs = {t.data_ptr(): t for t in keep}
+    att = m.layers[1].attention
+    qkv = ptrs[layers[1].qkv_weight]
+    assert qkv.dtype == torch.float16 and qkv.shape == (192, 64)
+    ref = torch.cat((att.q_proj.weight, att.k_proj.weight, att.v_proj.weight)).half()
+    assert torch.equal(qkv, ref)
+    bias = ptrs[layers[1].qkv_bias]
+    assert bias.dtype == torch.float32 and torch.equal(
+        bias, torch.cat((att.q_proj.bias, att.k_proj.bias, att.v_proj.bias)))
+    w1 = ptrs[layers[0].ffn_in_weight]
+    assert w1.shape == (96, 64) and w1.dtype == torch.float16
+    # cache hit on an unchanged model, repack after an in-place update
+    assert m._prepare(torch.device("cpu"))[0] == key
+    with torch.no_grad():
+        m.layers[0].ffn_in.weight.add_(1.0)
+    assert m._prepare(torch.device("cpu"))[0] != key
+
+
+def test_mask_handling(pkg):
+    cfg = pkg.TransformerConfig(3, 8, 64, 4, 64, 1, True)
+    m = pkg.UserOptimizedTransformer(cfg)
+    x = torch.zeros(3, 8, 64)
+    assert m._valid_lengths(x, None) is None
+    assert m._valid_lengths(x, torch.ones(3, 8, dtype=torch.bool)) is None
+    mask = torch.arange(8)[None, :] < torch.tensor([8, 5, 1])[:, None]
+    lengths = m._valid_lengths(x, mask)
+    assert lengths.dtype == torch.int32 and lengths.tolist() == [8, 5, 1]
+    holes = mask.clone()
+    holes[0, 3] = False
+    with pytest.raises(NotImplementedError):
+        m._valid_lengths(x, holes)
+    with pytest.raises(ValueError):
+        m._valid_lengths(x, torch.ones(3, 7, dtype=torch.bool))
+
+
+def test_no_cpu_fallback(pkg):
+    m = pkg.UserOptimizedTransformer(pkg.TransformerConfig(1, 8, 128, 4, 128, 1, True))
+    with pytest.raises(RuntimeError):
+        m(torch.zeros(1, 8, 128))
+    with pytest.raises(NotImplementedError):
+        pkg.BaselineTransformer(pkg.TransformerConfig(1, 8, 128, 4, 128, 1, True))(
+            torch.zeros(1, 8, 128))
+
+
+def test_toggles_keep_reference_contract(pkg):
+    m = pkg.UserOptimizedTransformer(pkg.TransformerConfig(1, 8, 128, 4, 128, 1, True))
+    m.enable_mixed_precision(torch.float16)
+    with pytest.warns(UserWarning):
+        m.enable_mixed_precision(torch.bfloat16)
+    with pytest.raises(ValueError):
+        m.enable_mixed_precision(torch.float64)
+    with pytest.raises(ValueError):
+        m.enable_attention_fp16_accumulation(True)
+    m.enable_attention_fp16_accumulation(False)
+    m.enable_triton_fused_norm(True)
+    m.enable_triton_fused_ffn(True)
+    with pytest.raises(NotImplementedError):
+        m.enable_kv_cache(True)
+
+
+def test_ops_reject_cpu_tensors(pkg):
+    x = torch.zeros(4, 128)
+    with pytest.raises(ValueError):
+        pkg.ops.layer_norm(x, torch.ones(128), torch.zeros(128), 1e-5, torch.float16)
+    with pytest.raises(ValueError):
+        pkg.ops.linear(x.half(), torch.zeros(32, 128).half(), torch.zeros(32))
