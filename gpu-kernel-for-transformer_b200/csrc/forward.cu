@@ -33,6 +33,12 @@ __global__ void zero_padded_rows_kernel(float* y, int seq, int d, const int32_t*
 }
 
 constexpr size_t kAlign = 256;
+int g_fused_policy = 1;  // 1: fused whole-forward kernel where it applies; 0: per-op chain
+
+bool use_fused(const tfx_model* m, int seq, const int32_t* valid_len) {
+  return g_fused_policy != 0 && fused_forward_supported(m, seq, valid_len);
+}
+
 size_t round_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 
 struct Workspace {
@@ -93,8 +99,15 @@ using namespace tfx;
 
 extern "C" {
 
+int tfx_set_fused_policy(int enable) {
+  const int prev = g_fused_policy;
+  g_fused_policy = enable ? 1 : 0;
+  return prev;
+}
+
 int64_t tfx_forward_workspace_bytes(const tfx_model* model, int batch, int seq) {
   if (check_model(model) != TFX_OK || batch <= 0 || seq <= 0) return -1;
+  if (use_fused(model, seq, nullptr)) return 0;
   const int64_t m = static_cast<int64_t>(batch) * seq;
   return static_cast<int64_t>(plan_workspace(nullptr, m, model->d_model, model->ffn_dim).bytes);
 }
@@ -104,14 +117,19 @@ int tfx_forward(const tfx_model* model, const float* x, float* y, int batch, int
                 tfx_stream_t stream_) {
   int st = check_model(model);
   if (st != TFX_OK) return st;
-  if (x == nullptr || y == nullptr || workspace == nullptr)
-    return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward: null x, y or workspace");
+  if (x == nullptr || y == nullptr)
+    return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward: null x or y");
   if (batch <= 0 || seq <= 0)
     return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward: batch and seq must be positive");
   if (x == y) return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward: y must not alias x");
   if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(y) % 16 ||
       reinterpret_cast<uintptr_t>(workspace) % kAlign)
     return fail(TFX_ERR_MISALIGNED, "tfx_forward: x/y 16-byte and workspace 256-byte alignment");
+  if (use_fused(model, seq, valid_len))
+    return launch_fused_forward(model, x, y, batch, seq, valid_len,
+                                reinterpret_cast<cudaStream_t>(stream_));
+  if (workspace == nullptr)
+    return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward: null workspace");
   const int64_t m = static_cast<int64_t>(batch) * seq;
   const int d = model->d_model, f = model->ffn_dim, nh = model->num_heads, hd = d / nh;
   const Workspace ws = plan_workspace(static_cast<char*>(workspace), m, d, f);

@@ -1,0 +1,611 @@
+// Whole-forward fused kernel for the narrow configs: d_model = ffn_dim = 128,
+// seq_len dividing 128, head_dim in {16, 32, 64, 128}, with or without a
+// prefix padding mask (per-sequence valid lengths).
+//
+// A tile is 128 consecutive token rows = 128/seq_len whole sequences, so
+// attention never leaves the tile. One persistent CTA per SM takes tiles
+// round-robin and carries each through ALL layers and the final LayerNorm
+// with every intermediate on chip: HBM sees the fp32 input once and the fp32
+// output once (1 KB per token), instead of ~27 KB per token for the chain of
+// separate kernels. Weights (192 KB fp16 per layer) stream from L2 through a
+// TMA ring.
+//
+// Roles (192 threads):
+//   warp 0      TMA producer: per layer Wq, Wk, Wv, Wo, W1, W2 (128x128 fp16
+//               each, 128-byte swizzle) into a 3-slot ring
+//   warp 1      TMEM owner (all 512 columns) + single-thread tcgen05.mma issuer
+//   warps 2..5  compute: thread t owns token row 32*(warp%4)+lane of the tile
+//               and does every row-wise step (LayerNorms, bias, GELU, softmax,
+//               residual adds) straight out of TMEM
+//
+// Per layer (c = compute warps, m = MMA thread; each step is an mbarrier
+// hand-off to the other side):
+//   c: LN1(x) -> sA                                     (fp16, K-major SW128)
+//   m: acc[0,384) = sA . [Wq;Wk;Wv]^T                   (three N=128 GEMMs)
+//   c: +bias -> Q into sA, K into sK, V^T into sV       (fp16)
+//   m: S = Q_h . K_h^T -> TMEM[0,128)
+//   c: masked softmax row -> P (fp16, normalised) into sP
+//   m: O[128 + h*hd, +hd) = P . V_h ; S_{h+1} = ...     (per head)
+//   c: ctx = O -> sP
+//   m: acc[0,128) = ctx . Wo^T
+//   c: x += acc + bo (fp32, kept in TMEM[384,512)); LN2(x) -> sP
+//   m: acc[128,256) = h2 . W1^T
+//   c: g = gelu_erf(acc + b1) -> sP
+//   m: acc[0,128) = g . W2^T
+//   c: x += acc + b2; next layer's LN1, or final LN -> y (global, fp32)
+//
+// tcgen05.ld/st are warp-collective: every TMEM access of the compute warps
+// is executed by all 32 lanes; rows past the end of the batch and padded
+// tokens are handled by predicating only the global stores.
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace tfx {
+
+constexpr int kFusedMaxLayers = 8;
+
+struct FusedParams {
+  CUtensorMap w_qkv[kFusedMaxLayers];
+  CUtensorMap w_out[kFusedMaxLayers];
+  CUtensorMap w_in[kFusedMaxLayers];
+  CUtensorMap w_fo[kFusedMaxLayers];
+  const float* b_qkv[kFusedMaxLayers];
+  const float* b_out[kFusedMaxLayers];
+  const float* b_in[kFusedMaxLayers];
+  const float* b_fo[kFusedMaxLayers];
+  const float* ln1_g[kFusedMaxLayers];
+  const float* ln1_b[kFusedMaxLayers];
+  const float* ln2_g[kFusedMaxLayers];
+  const float* ln2_b[kFusedMaxLayers];
+  const float* lnf_g;
+  const float* lnf_b;
+  const float* x;
+  float* y;
+  const int32_t* valid_len;  // nullable: [batch] prefix lengths (padding mask)
+  int64_t rows;
+  int num_layers;
+  int seq;
+  int num_tiles;
+  int causal;
+  float eps;
+  float scale_log2;
+  int* err;
+};
+
+namespace {
+
+constexpr int kT = 128;                      // tokens per tile = d_model = ffn_dim
+constexpr int kOpBytes = kT * kT * 2;        // one 128x128 fp16 operand (32 KB)
+constexpr int kBlkBytes = kT * 64 * 2;       // one 128-row x 64-col SW128 block (16 KB)
+constexpr int kWSlots = 3;
+constexpr int kOffA = 0;
+constexpr int kOffK = kOpBytes;
+constexpr int kOffV = 2 * kOpBytes;
+constexpr int kOffP = 3 * kOpBytes;
+constexpr int kOffW = 4 * kOpBytes;
+constexpr int kOffBar = kOffW + kWSlots * kOpBytes;
+constexpr int kSmemBytes = kOffBar + 128 + 1024;
+constexpr int kThreads = 192;
+constexpr uint32_t kColS = 0;    // attention scores (per head)
+constexpr uint32_t kColO = 128;  // attention output, all heads
+constexpr uint32_t kColF = 128;  // FFN-in accumulator
+constexpr uint32_t kColX = 384;  // fp32 residual stream of the tile
+
+// Byte address of row r, columns [c, c+8) of a K-major 128x128 fp16 operand
+// stored as two 128B-swizzled 64-column blocks (the layout TMA writes with
+// CU_TENSOR_MAP_SWIZZLE_128B and the MMA descriptors describe).
+__device__ __forceinline__ uint32_t sw_addr(uint32_t base, int r, int c) {
+  return base + static_cast<uint32_t>((c >> 6) * kBlkBytes + r * 128 +
+                                      ((((c & 63) >> 3) ^ (r & 7)) << 4));
+}
+
+__device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                       uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+}
+
+__device__ __forceinline__ void sts16(uint32_t addr, __half v) {
+  asm volatile("st.shared.b16 [%0], %1;" ::"r"(addr), "h"(__half_as_ushort(v)) : "memory");
+}
+
+// Row r, columns [c0, c0+32) of a K-major operand <- fp16(v).
+__device__ __forceinline__ void store_row32(uint32_t base, int r, int c0, const float* v) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    sts128(sw_addr(base, r, c0 + 8 * j), pack_half2(v[8 * j], v[8 * j + 1]),
+           pack_half2(v[8 * j + 2], v[8 * j + 3]), pack_half2(v[8 * j + 4], v[8 * j + 5]),
+           pack_half2(v[8 * j + 6], v[8 * j + 7]));
+  }
+}
+
+// V^T operand (rows = feature d, columns = key): write key row `key`,
+// features [d0, d0+32).
+__device__ __forceinline__ void store_vt32(uint32_t base, int key, int d0, const float* v) {
+  const uint32_t kb = static_cast<uint32_t>((key >> 6) * kBlkBytes + ((key & 7) << 1));
+  const int kc = (key & 63) >> 3;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const int d = d0 + j;
+    sts16(base + kb + static_cast<uint32_t>(d * 128 + ((kc ^ (d & 7)) << 4)),
+          __float2half_rn(v[j]));
+  }
+}
+
+__device__ __forceinline__ uint64_t op_desc(uint32_t base, int col) {
+  return sdesc_k_sw128(base + static_cast<uint32_t>((col >> 6) * kBlkBytes + (col & 63) * 2));
+}
+
+// D[128 x N] (+)= A[128 x K] . B[N x K]^T over k-steps of 16 starting at K
+// offsets a_col/b_col.
+__device__ __forceinline__ void mma_chain(uint32_t d, uint32_t a, int a_col, uint32_t b,
+                                          int b_col, int ksteps, uint32_t idesc) {
+  for (int k = 0; k < ksteps; ++k)
+    mma_f16_ss(d, op_desc(a, a_col + 16 * k), op_desc(b, b_col + 16 * k), idesc,
+               k > 0 ? 1u : 0u);
+}
+
+__device__ __forceinline__ void tmem_ld_row(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  tmem_ld32(taddr, r);
+  tmem_ld_wait();
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+__device__ __forceinline__ void add_bias32(float (&v)[32], const float* __restrict__ b) {
+  const float4* b4 = reinterpret_cast<const float4*>(b);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float4 t = __ldg(b4 + j);
+    v[4 * j] += t.x;
+    v[4 * j + 1] += t.y;
+    v[4 * j + 2] += t.z;
+    v[4 * j + 3] += t.w;
+  }
+}
+
+// LayerNorm statistics of the 128-wide fp32 row at TMEM `taddr` (this
+// thread's lane): mean, then the centred variance (as nn.LayerNorm), read
+// back from TMEM in 32-column chunks so the row never occupies registers.
+__device__ __forceinline__ void row_stats(uint32_t taddr, float eps, float& mean, float& rstd) {
+  float s = 0.f;
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    float v[32];
+    tmem_ld_row(taddr + 32 * c, v);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) s += v[j];
+  }
+  mean = s * (1.0f / 128.0f);
+  float q = 0.f;
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    float v[32];
+    tmem_ld_row(taddr + 32 * c, v);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const float t = v[j] - mean;
+      q = fmaf(t, t, q);
+    }
+  }
+  rstd = rsqrtf(q * (1.0f / 128.0f) + eps);
+}
+
+// Normalised, affine-transformed 32-column chunk c of the TMEM row.
+__device__ __forceinline__ void ln_chunk(uint32_t taddr, int c, float mean, float rstd,
+                                         const float* g, const float* b, float (&v)[32]) {
+  tmem_ld_row(taddr + 32 * c, v);
+  const float4* g4 = reinterpret_cast<const float4*>(g + 32 * c);
+  const float4* b4 = reinterpret_cast<const float4*>(b + 32 * c);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float4 gg = __ldg(g4 + j), bb = __ldg(b4 + j);
+    v[4 * j] = (v[4 * j] - mean) * rstd * gg.x + bb.x;
+    v[4 * j + 1] = (v[4 * j + 1] - mean) * rstd * gg.y + bb.y;
+    v[4 * j + 2] = (v[4 * j + 2] - mean) * rstd * gg.z + bb.z;
+    v[4 * j + 3] = (v[4 * j + 3] - mean) * rstd * gg.w + bb.w;
+  }
+}
+
+// LN of the TMEM row -> fp16 row r of K-major operand `base`.
+__device__ __forceinline__ void layer_norm_to_smem(uint32_t taddr, const float* g, const float* b,
+                                                   float eps, uint32_t base, int r) {
+  float mean, rstd;
+  row_stats(taddr, eps, mean, rstd);
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    float v[32];
+    ln_chunk(taddr, c, mean, rstd, g, b, v);
+    store_row32(base, r, 32 * c, v);
+  }
+}
+
+// LN of the TMEM row -> fp32 output row in global memory. The TMEM reads are
+// executed by the whole warp; `mode` only selects what is stored:
+// 0 = nothing (row past the end), 1 = the normalised row, 2 = zeros (padded token).
+__device__ __forceinline__ void layer_norm_to_global(uint32_t taddr, const float* g, const float* b,
+                                                     float eps, float* __restrict__ y, int mode) {
+  float mean, rstd;
+  row_stats(taddr, eps, mean, rstd);
+  float4* y4 = reinterpret_cast<float4*>(y);
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    float v[32];
+    ln_chunk(taddr, c, mean, rstd, g, b, v);
+    if (mode != 0) {
+      const float keep = mode == 1 ? 1.0f : 0.0f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        __stcs(y4 + 8 * c + j, make_float4(v[4 * j] * keep, v[4 * j + 1] * keep,
+                                           v[4 * j + 2] * keep, v[4 * j + 3] * keep));
+    }
+  }
+}
+
+// x[TMEM] += acc[TMEM] + bias, 32 columns at a time (fp32 residual add).
+__device__ __forceinline__ void residual_add(uint32_t t_x, uint32_t t_acc, const float* bias) {
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    float v[32], xr[32];
+    tmem_ld_row(t_acc + 32 * c, v);
+    tmem_ld_row(t_x + 32 * c, xr);
+    add_bias32(v, bias + 32 * c);
+    uint32_t o[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(v[j] + xr[j]);
+    tmem_st32(t_x + 32 * c, o);
+  }
+  tmem_st_wait();
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kThreads, 1)
+    fused_forward_kernel(const __grid_constant__ FusedParams p) {
+  constexpr int H = kT / HD;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t sA = sbase + kOffA, sK = sbase + kOffK, sV = sbase + kOffV, sP = sbase + kOffP;
+  uint64_t* w_full = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* w_empty = w_full + kWSlots;
+  uint64_t* c2m = w_empty + kWSlots;  // compute -> MMA hand-off (4 warp arrivals)
+  uint64_t* m2c = c2m + 1;            // MMA -> compute hand-off (tcgen05.commit)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(m2c + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kWSlots; ++s) {
+      mbar_init(&w_full[s], 1);
+      mbar_init(&w_empty[s], 1);
+    }
+    mbar_init(c2m, 4);
+    mbar_init(m2c, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int L = p.num_layers;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------- weight producer
+    int slot = 0;
+    uint32_t ph = 0;
+    int issued[kWSlots];
+    for (int s = 0; s < kWSlots; ++s) issued[s] = -1;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+      for (int l = 0; l < L && ok; ++l) {
+        for (int c = 0; c < 6; ++c) {
+          const CUtensorMap* m =
+              c < 3 ? &p.w_qkv[l] : (c == 3 ? &p.w_out[l] : (c == 4 ? &p.w_in[l] : &p.w_fo[l]));
+          const int row0 = c < 3 ? kT * c : 0;
+          if (!mbar_wait(&w_empty[slot], ph ^ 1, p.err, kDevTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          uint8_t* dst = smem + kOffW + slot * kOpBytes;
+          mbar_arrive_expect_tx(&w_full[slot], kOpBytes);
+          tma_load_2d(dst, m, &w_full[slot], 0, row0);
+          tma_load_2d(dst + kBlkBytes, m, &w_full[slot], 64, row0);
+          issued[slot] = static_cast<int>(ph);
+          if (++slot == kWSlots) {
+            slot = 0;
+            ph ^= 1;
+          }
+        }
+      }
+    }
+    if (!ok)  // unwinding after a timeout: let our own copies land first
+      for (int s = 0; s < kWSlots; ++s)
+        if (issued[s] >= 0) mbar_wait(&w_full[s], issued[s], nullptr, 0);
+  } else if (warp == 1 && lane == 0) {
+    // ----------------------------------------------------------- MMA issuer
+    constexpr uint32_t id128 = idesc_f16_f32(128, 128);
+    constexpr uint32_t idhd = idesc_f16_f32(128, HD);
+    int slot = 0;
+    uint32_t ph = 0, c2m_ph = 0;
+    auto wait_c2m = [&]() {
+      const bool r = mbar_wait(c2m, c2m_ph, p.err, kDevTimeoutOther);
+      c2m_ph ^= 1;
+      tc_fence_after();
+      return r;
+    };
+    auto gemm_w = [&](uint32_t dcol, uint32_t a) {
+      if (!mbar_wait(&w_full[slot], ph, p.err, kDevTimeoutFull)) return false;
+      tc_fence_after();
+      const uint32_t w = sbase + kOffW + static_cast<uint32_t>(slot * kOpBytes);
+      mma_chain(tmem + dcol, a, 0, w, 0, kT / 16, id128);
+      mma_commit(&w_empty[slot]);
+      if (++slot == kWSlots) {
+        slot = 0;
+        ph ^= 1;
+      }
+      return true;
+    };
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+      for (int l = 0; l < L && ok; ++l) {
+        ok = wait_c2m();  // LN1 output in sA
+        for (int c = 0; c < 3 && ok; ++c) ok = gemm_w(kT * c, sA);
+        if (!ok) break;
+        mma_commit(m2c);
+        if (!(ok = wait_c2m())) break;  // Q, K, V^T in smem
+        mma_chain(tmem + kColS, sA, 0, sK, 0, HD / 16, id128);
+        mma_commit(m2c);
+        for (int h = 0; h < H && ok; ++h) {
+          if (!(ok = wait_c2m())) break;  // P_h in sP
+          for (int k = 0; k < kT / 16; ++k)
+            mma_f16_ss(tmem + kColO + h * HD, op_desc(sP, 16 * k),
+                       op_desc(sV + static_cast<uint32_t>(h * HD * 128), 16 * k), idhd,
+                       k > 0 ? 1u : 0u);
+          if (h + 1 < H)
+            mma_chain(tmem + kColS, sA, (h + 1) * HD, sK, (h + 1) * HD, HD / 16, id128);
+          mma_commit(m2c);
+        }
+        if (!ok || !(ok = wait_c2m())) break;  // ctx in sP
+        if (!(ok = gemm_w(0, sP))) break;
+        mma_commit(m2c);
+        if (!(ok = wait_c2m())) break;  // LN2 output in sP
+        if (!(ok = gemm_w(kColF, sP))) break;
+        mma_commit(m2c);
+        if (!(ok = wait_c2m())) break;  // GELU output in sP
+        if (!(ok = gemm_w(0, sP))) break;
+        mma_commit(m2c);
+      }
+    }
+  } else if (warp >= 2) {
+    // ------------------------------------------------------------- compute
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    uint32_t m2c_ph = 0;
+    auto wait_m2c = [&]() {
+      // Warp-uniform outcome: a timeout seen by one lane ends the whole warp.
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(m2c, m2c_ph, p.err, kDevTimeoutAccum));
+      m2c_ph ^= 1;
+      tc_fence_after();
+      return ok;
+    };
+    auto signal = [&]() {
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(c2m);
+    };
+    const int S = p.seq;
+    // Key range of this thread's row (own sequence; causal) and the
+    // warp-uniform range of 32-key chunks that can hold a valid key.
+    const int seq_lo = (r / S) * S;
+    const int key_hi_nopad = p.causal ? r : seq_lo + S - 1;
+    const int ch_lo = (((q * 32) / S) * S) >> 5;
+    const int ch_hi = (p.causal ? (q * 32 + 31) : (((q * 32 + 31) / S) * S + S - 1)) >> 5;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+      const int64_t grow = static_cast<int64_t>(tile) * kT + r;
+      const bool row_ok = grow < p.rows;
+      const int len = (p.valid_len != nullptr && row_ok) ? p.valid_len[grow / S] : S;
+      const int key_hi = min(key_hi_nopad, seq_lo + len - 1);  // padded keys masked
+      const bool row_valid = (r - seq_lo) < len;                // not a padded token
+      {  // x row (fp32) -> TMEM residual columns
+        const float4* x4 = reinterpret_cast<const float4*>(p.x + grow * kT);
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 t = row_ok ? __ldcs(x4 + 8 * c + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+            o[4 * j] = __float_as_uint(t.x);
+            o[4 * j + 1] = __float_as_uint(t.y);
+            o[4 * j + 2] = __float_as_uint(t.z);
+            o[4 * j + 3] = __float_as_uint(t.w);
+          }
+          tmem_st32(tl + kColX + 32 * c, o);
+        }
+        tmem_st_wait();
+      }
+      for (int l = 0; l < L; ++l) {
+        layer_norm_to_smem(tl + kColX, p.ln1_g[l], p.ln1_b[l], p.eps, sA, r);
+        signal();
+        if (!(ok = wait_m2c())) break;
+        // QKV epilogue: bias, fp16, scatter into the attention operands.
+#pragma unroll 1
+        for (int c = 0; c < 12; ++c) {
+          float v[32];
+          tmem_ld_row(tl + 32 * c, v);
+          add_bias32(v, p.b_qkv[l] + 32 * c);
+          if (c < 4)
+            store_row32(sA, r, 32 * c, v);
+          else if (c < 8)
+            store_row32(sK, r, 32 * (c - 4), v);
+          else
+            store_vt32(sV, r, 32 * (c - 8), v);
+        }
+        signal();
+        // Attention, one head at a time. P is normalised before P.V, so the
+        // attention output needs no rescaling afterwards.
+#pragma unroll 1
+        for (int h = 0; h < H; ++h) {
+          if (!(ok = wait_m2c())) break;
+          float sc[4][32];
+          float mx = -INFINITY;
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch) {
+            if (ch >= ch_lo && ch <= ch_hi) {  // warp-uniform
+              tmem_ld_row(tl + kColS + 32 * ch, sc[ch]);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const int key = 32 * ch + j;
+                const bool valid = key >= seq_lo && key <= key_hi;
+                sc[ch][j] = valid ? sc[ch][j] * p.scale_log2 : -INFINITY;
+                mx = fmaxf(mx, sc[ch][j]);
+              }
+            }
+          }
+          // A row whose keys are all padding (zero-length sequence) has
+          // mx = -inf: use 0 so every weight is exp2(-inf) = 0, never NaN.
+          if (mx == -INFINITY) mx = 0.f;
+          float sum = 0.f;
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch) {
+            if (ch >= ch_lo && ch <= ch_hi) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                sc[ch][j] = exp2f(sc[ch][j] - mx);
+                sum += sc[ch][j];
+              }
+            }
+          }
+          const float inv = sum > 0.f ? 1.0f / sum : 0.f;
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch) {
+            if (ch >= ch_lo && ch <= ch_hi) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) sc[ch][j] *= inv;
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) sc[ch][j] = 0.f;
+            }
+            store_row32(sP, r, 32 * ch, sc[ch]);
+          }
+          signal();
+        }
+        if (!ok || !(ok = wait_m2c())) break;  // last P.V done
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float v[32];
+          tmem_ld_row(tl + kColO + 32 * c, v);
+          store_row32(sP, r, 32 * c, v);
+        }
+        signal();
+        if (!(ok = wait_m2c())) break;  // out-proj accumulator
+        residual_add(tl + kColX, tl, p.b_out[l]);
+        layer_norm_to_smem(tl + kColX, p.ln2_g[l], p.ln2_b[l], p.eps, sP, r);
+        signal();
+        if (!(ok = wait_m2c())) break;  // FFN-in accumulator
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float v[32];
+          tmem_ld_row(tl + kColF + 32 * c, v);
+          add_bias32(v, p.b_in[l] + 32 * c);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
+          store_row32(sP, r, 32 * c, v);
+        }
+        signal();
+        if (!(ok = wait_m2c())) break;  // FFN-out accumulator
+        residual_add(tl + kColX, tl, p.b_fo[l]);
+        if (l + 1 == L)
+          layer_norm_to_global(tl + kColX, p.lnf_g, p.lnf_b, p.eps, p.y + grow * kT,
+                               row_ok ? (row_valid ? 1 : 2) : 0);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+}  // namespace
+
+bool fused_forward_supported(const tfx_model* m, int seq, const int32_t* /*valid_len*/) {
+  if (m->d_model != kT || m->ffn_dim != kT) return false;
+  if (m->num_layers > kFusedMaxLayers || seq <= 0 || kT % seq != 0) return false;
+  const int hd = m->d_model / m->num_heads;
+  return hd == 16 || hd == 32 || hd == 64 || hd == 128;
+}
+
+int launch_fused_forward(const tfx_model* m, const float* x, float* y, int batch, int seq,
+                         const int32_t* valid_len, cudaStream_t stream) {
+  FusedParams p;
+  memset(&p, 0, sizeof(p));
+  for (int l = 0; l < m->num_layers; ++l) {
+    const tfx_layer& Ly = m->layers[l];
+    int st = make_tmap_2d(&p.w_qkv[l], Ly.qkv_weight, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, 3 * kT,
+                          kT, kT, 64, kT, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st == TFX_OK)
+      st = make_tmap_2d(&p.w_out[l], Ly.out_weight, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, kT, kT,
+                        kT, 64, kT, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st == TFX_OK)
+      st = make_tmap_2d(&p.w_in[l], Ly.ffn_in_weight, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, kT, kT,
+                        kT, 64, kT, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st == TFX_OK)
+      st = make_tmap_2d(&p.w_fo[l], Ly.ffn_out_weight, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, kT, kT,
+                        kT, 64, kT, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != TFX_OK) return st;
+    p.b_qkv[l] = Ly.qkv_bias;
+    p.b_out[l] = Ly.out_bias;
+    p.b_in[l] = Ly.ffn_in_bias;
+    p.b_fo[l] = Ly.ffn_out_bias;
+    p.ln1_g[l] = Ly.norm1_weight;
+    p.ln1_b[l] = Ly.norm1_bias;
+    p.ln2_g[l] = Ly.norm2_weight;
+    p.ln2_b[l] = Ly.norm2_bias;
+  }
+  p.lnf_g = m->final_norm_weight;
+  p.lnf_b = m->final_norm_bias;
+  p.x = x;
+  p.y = y;
+  p.valid_len = valid_len;
+  p.rows = static_cast<int64_t>(batch) * seq;
+  p.num_layers = m->num_layers;
+  p.seq = seq;
+  p.num_tiles = static_cast<int>((p.rows + kT - 1) / kT);
+  p.causal = m->causal;
+  p.eps = m->eps;
+  const int hd = m->d_model / m->num_heads;
+  p.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(hd));
+  p.err = device_error_word();
+  const int grid = p.num_tiles < num_sms() ? p.num_tiles : num_sms();
+  int st = TFX_OK;
+#define TFX_FUSED_CASE(HDV)                                                                     \
+  case HDV: {                                                                                   \
+    static int done[kMaxDevices] = {0};                                                         \
+    st = ensure_smem(reinterpret_cast<const void*>(fused_forward_kernel<HDV>), kSmemBytes, done); \
+    if (st != TFX_OK) return st;                                                                \
+    fused_forward_kernel<HDV><<<grid, kThreads, kSmemBytes, stream>>>(p);                       \
+    break;                                                                                      \
+  }
+  switch (hd) {
+    TFX_FUSED_CASE(16)
+    TFX_FUSED_CASE(32)
+    TFX_FUSED_CASE(64)
+    TFX_FUSED_CASE(128)
+    default:
+      return fail(TFX_ERR_UNSUPPORTED, "fused forward: head_dim %d", hd);
+  }
+#undef TFX_FUSED_CASE
+  return check_launch("fused_forward_kernel");
+}
+
+}  // namespace tfx

@@ -147,7 +147,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int buf = local & 1;
       const uint32_t use = static_cast<uint32_t>(local >> 1);
-      if (!mbar_wait(&acc_full[buf], use & 1, err, kDevTimeoutAccum)) break;
+      // Warp-uniform outcome (the TMEM loads below are warp-collective).
+      if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[buf], use & 1, err, kDevTimeoutAccum)))
+        break;
       tc_fence_after();
       const int m0 = (tile % tiles_m) * kBM;
       const int n0 = (tile / tiles_m) * BN;

@@ -7,6 +7,7 @@
 
 #include <cstdint>
 #include <cstdio>
+#include <cstring>
 #include <string>
 
 #include "../../include/tfx.h"
@@ -49,5 +50,10 @@ int launch_linear(const __half* a, int64_t lda, const __half* w, const float* bi
 int launch_attention(const __half* q, const __half* k, const __half* v, int64_t ld_qkv,
                      __half* out, int64_t ld_out, int batch, int heads, int seq, int head_dim,
                      float scale, int causal, const int32_t* valid_len, cudaStream_t stream);
+
+// Whole-forward fused kernel (d_model = ffn_dim = 128, seq | 128).
+bool fused_forward_supported(const tfx_model* m, int seq, const int32_t* valid_len);
+int launch_fused_forward(const tfx_model* m, const float* x, float* y, int batch, int seq,
+                         const int32_t* valid_len, cudaStream_t stream);
 
 }  // namespace tfx

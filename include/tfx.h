@@ -145,14 +145,27 @@ typedef struct tfx_model {
   const float* final_norm_bias;
 } tfx_model;
 
-/* Bytes of device workspace tfx_forward needs for a [batch, seq] input. */
+/*
+ * Path policy of tfx_forward for this process: 1 (default) runs the fused
+ * whole-forward kernel wherever it applies (d_model = ffn_dim = 128, seq_len
+ * dividing 128, head_dim in {16, 32, 64, 128}, <= 8 layers; with or without
+ * valid_len); 0 always runs the per-op kernel chain. Returns the previous
+ * policy. Query tfx_forward_workspace_bytes again after changing it.
+ * No reference counterpart (the reference's toggles are per-module:
+ * enable_triton_fused_norm / _ffn, torch_transformer_benchmark.py:379-393).
+ */
+TFX_API int tfx_set_fused_policy(int enable);
+
+/* Bytes of device workspace tfx_forward needs for a [batch, seq] input
+ * (0 when the fused whole-forward kernel applies). */
 TFX_API int64_t tfx_forward_workspace_bytes(const tfx_model* model, int batch, int seq);
 
 /*
  * Whole forward: y = final_norm(blocks(x)), x and y [batch, seq, D] fp32
  * (y must not alias x). valid_len: NULL or [batch] int32 prefix lengths
  * (padded rows of y are zeroed, padded keys masked). workspace: device
- * buffer of at least tfx_forward_workspace_bytes().
+ * buffer of at least tfx_forward_workspace_bytes() (may be NULL when that
+ * is 0).
  * Replaces: UserOptimizedTransformer.forward -> _forward_cuda ->
  * _forward_cuda_fused_norm (torch_transformer_benchmark.py:996-1020,
  * :1051-1090, :1092-1148).

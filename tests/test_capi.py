@@ -100,6 +100,15 @@ def test_workspace_size_formula(lib):
     m.layers = ctypes.cast(layers, ctypes.POINTER(L.TfxLayer))
     m.final_norm_weight = m.final_norm_bias = 256
     rows = 10 * 128
-    need = lib.tfx_forward_workspace_bytes(ctypes.byref(m), 10, 128)
+    per_row = 2 * 128 + 2 * 384 + 2 * 128 + 4 * 128 + 2 * 128
+    # D = F = 128, seq | 128: the fused whole-forward kernel needs no workspace
+    assert lib.tfx_forward_workspace_bytes(ctypes.byref(m), 10, 128) == 0
+    prev = lib.tfx_set_fused_policy(0)
+    try:
+        need = lib.tfx_forward_workspace_bytes(ctypes.byref(m), 10, 128)
+    finally:
+        lib.tfx_set_fused_policy(prev)
     # h, qkv, ctx (fp16, D, 3D, D) + residual (fp32, D) + ffn hidden (fp16, F)
-    assert need == rows * (2 * 128 + 2 * 384 + 2 * 128 + 4 * 128 + 2 * 128)
+    assert need == rows * per_row
+    # seq not dividing 128: the per-op chain and its workspace
+    assert lib.tfx_forward_workspace_bytes(ctypes.byref(m), 10, 100) == 1000 * per_row

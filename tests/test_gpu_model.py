@@ -114,3 +114,56 @@ def test_graph_replay_matches_eager(pkg, dev):
 def test_no_device_timeout_recorded(pkg, dev):
     torch.cuda.synchronize()
     assert pkg._lib.read_device_error() == 0
+
+
+FUSED_CASES = [
+    # (batch, seq, d_model, heads, ffn, layers, causal[, padding_ratio])
+    (4, 128, 128, 4, 128, 4, True),     # c1
+    (300, 128, 128, 4, 128, 4, True),   # c2 geometry, several tiles per CTA
+    (3, 128, 128, 8, 128, 2, True),     # head_dim 16
+    (3, 128, 128, 2, 128, 2, True),     # head_dim 64
+    (2, 128, 128, 1, 128, 2, True),     # head_dim 128
+    (5, 32, 128, 4, 128, 2, True),      # 4 sequences per tile, partial last tile
+    (7, 1, 128, 4, 128, 2, True),       # one token per sequence
+    (6, 64, 128, 4, 128, 2, False),     # non-causal, block-diagonal tiles
+    (2, 16, 128, 4, 128, 3, True),
+    (9, 128, 128, 4, 128, 2, True, 0.5),   # prefix padding masks
+    (9, 32, 128, 4, 128, 2, False, 0.6),
+]
+
+
+@pytest.mark.parametrize("case", FUSED_CASES)
+def test_fused_forward_and_op_chain_match_oracle(pkg, dev, case):
+    """The fused whole-forward kernel and the per-op kernel chain both pass
+    the rule against the oracle on the same weights and inputs."""
+    import ctypes
+
+    b, s, d, h, f, l, causal = case[:7]
+    pad = case[7] if len(case) > 7 else 0.0
+    kw = dict(batch_size=b, seq_len=s, d_model=d, num_heads=h, ffn_dim=f, num_layers=l,
+              causal=causal)
+    oracle_model, cand = _pair(pkg, kw, 99, dev)
+    x, mask = ob.generate_random_case(ob.TransformerConfig(**kw), 5, pad)
+    lib = pkg._lib.load()
+    _, _, _, mdl = cand._prepare(dev)
+    outs = {}
+    try:
+        for policy in (1, 0):
+            lib.tfx_set_fused_policy(policy)
+            need = lib.tfx_forward_workspace_bytes(ctypes.byref(mdl), b, s)
+            assert (need == 0) == (policy == 1), need
+            with torch.inference_mode():
+                outs[policy] = cand(x.to(dev), mask.to(dev)).cpu()
+    finally:
+        lib.tfx_set_fused_policy(1)
+    with torch.inference_mode():
+        ref = oracle_model(x, mask)
+    for policy, y in outs.items():
+        res = ob.compare_outputs(ref, y, RTOL, ATOL)
+        assert res.failed_elements == 0, (case, policy, res.failed_elements, res.max_abs_error)
+    assert (outs[0] - outs[1]).abs().max() < 2e-3
+
+
+def test_no_device_timeout_after_fused(pkg, dev):
+    torch.cuda.synchronize()
+    assert pkg._lib.read_device_error() == 0
