@@ -175,6 +175,23 @@ TFX_API int tfx_forward(const tfx_model* model, const float* x, float* y, int ba
                 tfx_stream_t stream);
 
 /*
+ * tfx_forward without a workspace argument, for callers that cannot allocate
+ * device memory (plugins whose host runtime owns all GPU memory, FFI
+ * bindings that can pass only the input and output buffers, serving loops
+ * that must not allocate after start-up). The per-op kernel chain's
+ * intermediates live in a fixed 32 MiB device array inside this library,
+ * held on every GPU that loads it until the process exits; calls whose
+ * tfx_forward_workspace_bytes() exceeds 32 MiB return TFX_ERR_WORKSPACE
+ * before anything is enqueued. All calls on a device share that array:
+ * calls that overlap on the GPU (unordered streams, several threads) race.
+ * The array need not be cleared between calls. The first call on each
+ * device looks up the array's device address, so make it before any stream
+ * capture. No counterpart in the reference.
+ */
+TFX_API int tfx_forward_static(const tfx_model* model, const float* x, float* y, int batch,
+                               int seq, const int32_t* valid_len, tfx_stream_t stream);
+
+/*
  * Reads and clears the calling device's kernel error word (synchronises the
  * device). *code receives 0 or a timeout code; returns TFX_OK or TFX_ERR_CUDA.
  * No reference counterpart (the reference's kernels have no waits).
