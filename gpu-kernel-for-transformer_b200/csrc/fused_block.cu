@@ -10,13 +10,17 @@
 // separate kernels. Weights (192 KB fp16 per layer) stream from L2 through a
 // TMA ring.
 //
-// Roles (192 threads):
+// Roles (320 threads):
 //   warp 0      TMA producer: per layer Wq, Wk, Wv, Wo, W1, W2 (128x128 fp16
 //               each, 128-byte swizzle) into a 3-slot ring
 //   warp 1      TMEM owner (all 512 columns) + single-thread tcgen05.mma issuer
-//   warps 2..5  compute: thread t owns token row 32*(warp%4)+lane of the tile
-//               and does every row-wise step (LayerNorms, bias, GELU, softmax,
-//               residual adds) straight out of TMEM
+//   warps 2..9  compute, two warps per TMEM lane quarter: lane l of warp w
+//               owns token row 32*(w%4)+l of the tile and HALF of its columns
+//               (half = (w-2)/4: columns / keys [64*half, 64*half+64)), and
+//               does every row-wise step (LayerNorms, bias, GELU, softmax,
+//               residual adds) straight out of TMEM. Row reductions (LN
+//               statistics, softmax max) are combined with the partner warp
+//               through free TMEM columns and a 64-thread named barrier.
 //
 // Per layer (c = compute warps, m = MMA thread; each step is an mbarrier
 // hand-off to the other side):
@@ -24,9 +28,10 @@
 //   m: acc[0,384) = sA . [Wq;Wk;Wv]^T                   (three N=128 GEMMs)
 //   c: +bias -> Q into sA, K into sK, V^T into sV       (fp16)
 //   m: S = Q_h . K_h^T -> TMEM[0,128)
-//   c: masked softmax row -> P (fp16, normalised) into sP
+//   c: masked softmax row -> P = exp2(s - max) (fp16, <= 1) into sP;
+//      the row sum goes to TMEM
 //   m: O[128 + h*hd, +hd) = P . V_h ; S_{h+1} = ...     (per head)
-//   c: ctx = O -> sP
+//   c: ctx = O / rowsum -> sP
 //   m: acc[0,128) = ctx . Wo^T
 //   c: x += acc + bo (fp32, kept in TMEM[384,512)); LN2(x) -> sP
 //   m: acc[128,256) = h2 . W1^T
@@ -85,11 +90,15 @@ constexpr int kOffP = 3 * kOpBytes;
 constexpr int kOffW = 4 * kOpBytes;
 constexpr int kOffBar = kOffW + kWSlots * kOpBytes;
 constexpr int kSmemBytes = kOffBar + 128 + 1024;
-constexpr int kThreads = 192;
-constexpr uint32_t kColS = 0;    // attention scores (per head)
-constexpr uint32_t kColO = 128;  // attention output, all heads
-constexpr uint32_t kColF = 128;  // FFN-in accumulator
-constexpr uint32_t kColX = 384;  // fp32 residual stream of the tile
+constexpr int kComputeWarps = 8;
+constexpr int kThreads = 32 * (2 + kComputeWarps);
+constexpr uint32_t kColS = 0;      // attention scores (per head)
+constexpr uint32_t kColO = 128;    // attention output, all heads
+constexpr uint32_t kColF = 128;    // FFN-in accumulator
+constexpr uint32_t kColXch = 256;  // pair-exchange slots (free once the QKV
+                                   // epilogue has read the V accumulator)
+constexpr uint32_t kColSum = 320;  // per-head partial softmax sums
+constexpr uint32_t kColX = 384;    // fp32 residual stream of the tile
 
 // Byte address of row r, columns [c, c+8) of a K-major 128x128 fp16 operand
 // stored as two 128B-swizzled 64-column blocks (the layout TMA writes with
@@ -166,96 +175,121 @@ __device__ __forceinline__ void add_bias32(float (&v)[32], const float* __restri
   }
 }
 
-// LayerNorm statistics of the 128-wide fp32 row at TMEM `taddr` (this
-// thread's lane): mean, then the centred variance (as nn.LayerNorm), read
-// back from TMEM in 32-column chunks so the row never occupies registers.
-__device__ __forceinline__ void row_stats(uint32_t taddr, float eps, float& mean, float& rstd) {
+// Per-row partial (sum or max) of this warp combined with the partner warp
+// that owns the other half of the same rows: written to TMEM column
+// kColXch + 2*slot + half, read back from the partner's column after a
+// 64-thread named barrier. Both warps get the identical result.
+template <bool IS_MAX>
+__device__ __forceinline__ float pair_combine(uint32_t tl, int slot, int half, int bar_id,
+                                              float mine) {
+  tmem_st1(tl + kColXch + 2 * slot + half, __float_as_uint(mine));
+  tmem_st_wait();
+  tc_fence_before();
+  named_bar_sync(bar_id, 64);
+  tc_fence_after();
+  uint32_t o;
+  tmem_ld1(tl + kColXch + 2 * slot + (half ^ 1), o);
+  tmem_ld_wait();
+  const float other = __uint_as_float(o);
+  return IS_MAX ? fmaxf(mine, other) : mine + other;
+}
+
+// Mean and rstd of the full 128-wide row from this warp's 64 values.
+__device__ __forceinline__ void pair_row_stats(const float (&x)[2][32], uint32_t tl, int& slot,
+                                               int half, int bar_id, float eps, float& mean,
+                                               float& rstd) {
   float s = 0.f;
-#pragma unroll 1
-  for (int c = 0; c < 4; ++c) {
-    float v[32];
-    tmem_ld_row(taddr + 32 * c, v);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) s += v[j];
-  }
-  mean = s * (1.0f / 128.0f);
+  for (int c = 0; c < 2; ++c)
+#pragma unroll
+    for (int j = 0; j < 32; ++j) s += x[c][j];
+  mean = pair_combine<false>(tl, slot++, half, bar_id, s) * (1.0f / 128.0f);
   float q = 0.f;
-#pragma unroll 1
-  for (int c = 0; c < 4; ++c) {
-    float v[32];
-    tmem_ld_row(taddr + 32 * c, v);
+#pragma unroll
+  for (int c = 0; c < 2; ++c)
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
-      const float t = v[j] - mean;
+      const float t = x[c][j] - mean;
       q = fmaf(t, t, q);
     }
-  }
-  rstd = rsqrtf(q * (1.0f / 128.0f) + eps);
+  rstd = rsqrtf(pair_combine<false>(tl, slot++, half, bar_id, q) * (1.0f / 128.0f) + eps);
 }
 
-// Normalised, affine-transformed 32-column chunk c of the TMEM row.
-__device__ __forceinline__ void ln_chunk(uint32_t taddr, int c, float mean, float rstd,
-                                         const float* g, const float* b, float (&v)[32]) {
-  tmem_ld_row(taddr + 32 * c, v);
-  const float4* g4 = reinterpret_cast<const float4*>(g + 32 * c);
-  const float4* b4 = reinterpret_cast<const float4*>(b + 32 * c);
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const float4 gg = __ldg(g4 + j), bb = __ldg(b4 + j);
-    v[4 * j] = (v[4 * j] - mean) * rstd * gg.x + bb.x;
-    v[4 * j + 1] = (v[4 * j + 1] - mean) * rstd * gg.y + bb.y;
-    v[4 * j + 2] = (v[4 * j + 2] - mean) * rstd * gg.z + bb.z;
-    v[4 * j + 3] = (v[4 * j + 3] - mean) * rstd * gg.w + bb.w;
-  }
-}
-
-// LN of the TMEM row -> fp16 row r of K-major operand `base`.
-__device__ __forceinline__ void layer_norm_to_smem(uint32_t taddr, const float* g, const float* b,
-                                                   float eps, uint32_t base, int r) {
+// LayerNorm of the row (this warp's half in registers) -> fp16 columns
+// [64*half, +64) of row r of K-major operand `base`.
+__device__ __forceinline__ void pair_ln_to_smem(const float (&x)[2][32], uint32_t tl, int& slot,
+                                                int half, int bar_id, float eps, const float* g,
+                                                const float* b, uint32_t base, int r) {
   float mean, rstd;
-  row_stats(taddr, eps, mean, rstd);
-#pragma unroll 1
-  for (int c = 0; c < 4; ++c) {
+  pair_row_stats(x, tl, slot, half, bar_id, eps, mean, rstd);
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    const int col = 64 * half + 32 * c;
+    const float4* g4 = reinterpret_cast<const float4*>(g + col);
+    const float4* b4 = reinterpret_cast<const float4*>(b + col);
     float v[32];
-    ln_chunk(taddr, c, mean, rstd, g, b, v);
-    store_row32(base, r, 32 * c, v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 gg = __ldg(g4 + j), bb = __ldg(b4 + j);
+      v[4 * j] = (x[c][4 * j] - mean) * rstd * gg.x + bb.x;
+      v[4 * j + 1] = (x[c][4 * j + 1] - mean) * rstd * gg.y + bb.y;
+      v[4 * j + 2] = (x[c][4 * j + 2] - mean) * rstd * gg.z + bb.z;
+      v[4 * j + 3] = (x[c][4 * j + 3] - mean) * rstd * gg.w + bb.w;
+    }
+    store_row32(base, r, col, v);
   }
 }
 
-// LN of the TMEM row -> fp32 output row in global memory. The TMEM reads are
-// executed by the whole warp; `mode` only selects what is stored:
-// 0 = nothing (row past the end), 1 = the normalised row, 2 = zeros (padded token).
-__device__ __forceinline__ void layer_norm_to_global(uint32_t taddr, const float* g, const float* b,
-                                                     float eps, float* __restrict__ y, int mode) {
+// Final LayerNorm -> fp32 output columns [64*half, +64) of the row. mode:
+// 0 = store nothing (row past the batch), 1 = the row, 2 = zeros (padded token).
+__device__ __forceinline__ void pair_ln_to_global(const float (&x)[2][32], uint32_t tl, int& slot,
+                                                  int half, int bar_id, float eps, const float* g,
+                                                  const float* b, float* __restrict__ y,
+                                                  int mode) {
   float mean, rstd;
-  row_stats(taddr, eps, mean, rstd);
-  float4* y4 = reinterpret_cast<float4*>(y);
-#pragma unroll 1
-  for (int c = 0; c < 4; ++c) {
-    float v[32];
-    ln_chunk(taddr, c, mean, rstd, g, b, v);
-    if (mode != 0) {
-      const float keep = mode == 1 ? 1.0f : 0.0f;
+  pair_row_stats(x, tl, slot, half, bar_id, eps, mean, rstd);
+  if (mode == 0) return;
+  const float keep = mode == 1 ? 1.0f : 0.0f;
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
-        __stcs(y4 + 8 * c + j, make_float4(v[4 * j] * keep, v[4 * j + 1] * keep,
-                                           v[4 * j + 2] * keep, v[4 * j + 3] * keep));
+  for (int c = 0; c < 2; ++c) {
+    const int col = 64 * half + 32 * c;
+    const float4* g4 = reinterpret_cast<const float4*>(g + col);
+    const float4* b4 = reinterpret_cast<const float4*>(b + col);
+    float4* y4 = reinterpret_cast<float4*>(y + col);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 gg = __ldg(g4 + j), bb = __ldg(b4 + j);
+      __stcs(y4 + j, make_float4(((x[c][4 * j] - mean) * rstd * gg.x + bb.x) * keep,
+                                 ((x[c][4 * j + 1] - mean) * rstd * gg.y + bb.y) * keep,
+                                 ((x[c][4 * j + 2] - mean) * rstd * gg.z + bb.z) * keep,
+                                 ((x[c][4 * j + 3] - mean) * rstd * gg.w + bb.w) * keep));
     }
   }
 }
 
-// x[TMEM] += acc[TMEM] + bias, 32 columns at a time (fp32 residual add).
-__device__ __forceinline__ void residual_add(uint32_t t_x, uint32_t t_acc, const float* bias) {
-#pragma unroll 1
-  for (int c = 0; c < 4; ++c) {
-    float v[32], xr[32];
-    tmem_ld_row(t_acc + 32 * c, v);
-    tmem_ld_row(t_x + 32 * c, xr);
-    add_bias32(v, bias + 32 * c);
-    uint32_t o[32];
+// x[TMEM, this warp's half] += acc + bias; the new values are also returned
+// in registers for the LayerNorm that always follows.
+__device__ __forceinline__ void pair_residual_add(uint32_t tl, uint32_t t_acc, int half,
+                                                  const float* bias, float (&x)[2][32]) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(v[j] + xr[j]);
-    tmem_st32(t_x + 32 * c, o);
+  for (int c = 0; c < 2; ++c) {
+    const int col = 64 * half + 32 * c;
+    uint32_t ra[32], rx[32];
+    tmem_ld32(t_acc + col, ra);
+    tmem_ld32(tl + kColX + col, rx);
+    tmem_ld_wait();
+    const float4* b4 = reinterpret_cast<const float4*>(bias + col);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 bb = __ldg(b4 + j);
+      x[c][4 * j] = __uint_as_float(rx[4 * j]) + (__uint_as_float(ra[4 * j]) + bb.x);
+      x[c][4 * j + 1] = __uint_as_float(rx[4 * j + 1]) + (__uint_as_float(ra[4 * j + 1]) + bb.y);
+      x[c][4 * j + 2] = __uint_as_float(rx[4 * j + 2]) + (__uint_as_float(ra[4 * j + 2]) + bb.z);
+      x[c][4 * j + 3] = __uint_as_float(rx[4 * j + 3]) + (__uint_as_float(ra[4 * j + 3]) + bb.w);
+    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j) rx[j] = __float_as_uint(x[c][j]);
+    tmem_st32(tl + kColX + col, rx);
   }
   tmem_st_wait();
 }
@@ -271,7 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t sA = sbase + kOffA, sK = sbase + kOffK, sV = sbase + kOffV, sP = sbase + kOffP;
   uint64_t* w_full = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* w_empty = w_full + kWSlots;
-  uint64_t* c2m = w_empty + kWSlots;  // compute -> MMA hand-off (4 warp arrivals)
+  uint64_t* c2m = w_empty + kWSlots;  // compute -> MMA hand-off (one arrival per compute warp)
   uint64_t* m2c = c2m + 1;            // MMA -> compute hand-off (tcgen05.commit)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(m2c + 1);
 
@@ -281,7 +315,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&w_full[s], 1);
       mbar_init(&w_empty[s], 1);
     }
-    mbar_init(c2m, 4);
+    mbar_init(c2m, kComputeWarps);
     mbar_init(m2c, 1);
     fence_mbar_init();
   }
@@ -384,7 +418,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= 2) {
     // ------------------------------------------------------------- compute
-    const int q = warp & 3;
+    constexpr int HPH = HD >= 64 ? 1 : 64 / HD;  // heads covering one column half
+    const int q = warp & 3;                       // TMEM lane quarter
+    const int half = (warp - 2) >> 2;             // column / key half
+    const int bar_id = 1 + q;                     // shared with the partner warp
     const int r = q * 32 + lane;
     const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16);
     uint32_t m2c_ph = 0;
@@ -408,6 +445,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int key_hi_nopad = p.causal ? r : seq_lo + S - 1;
     const int ch_lo = (((q * 32) / S) * S) >> 5;
     const int ch_hi = (p.causal ? (q * 32 + 31) : (((q * 32 + 31) / S) * S + S - 1)) >> 5;
+    const float sl2 = p.scale_log2;
     bool ok = true;
     for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
       const int64_t grow = static_cast<int64_t>(tile) * kT + r;
@@ -415,30 +453,38 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int len = (p.valid_len != nullptr && row_ok) ? p.valid_len[grow / S] : S;
       const int key_hi = min(key_hi_nopad, seq_lo + len - 1);  // padded keys masked
       const bool row_valid = (r - seq_lo) < len;                // not a padded token
-      {  // x row (fp32) -> TMEM residual columns
-        const float4* x4 = reinterpret_cast<const float4*>(p.x + grow * kT);
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
+      // A chunk needs no masking when every key in it is valid for every row
+      // of this warp: whole-tile sequences, no padding, below the diagonal.
+      const bool plain_tile = (S == kT) && (p.valid_len == nullptr);
+      int slot = 0;
+      float xv[2][32];  // this warp's 64 columns of the fp32 residual row
+      {
+        const float4* x4 = reinterpret_cast<const float4*>(p.x + grow * kT + 64 * half);
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
           uint32_t o[32];
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             const float4 t = row_ok ? __ldcs(x4 + 8 * c + j) : make_float4(0.f, 0.f, 0.f, 0.f);
-            o[4 * j] = __float_as_uint(t.x);
-            o[4 * j + 1] = __float_as_uint(t.y);
-            o[4 * j + 2] = __float_as_uint(t.z);
-            o[4 * j + 3] = __float_as_uint(t.w);
+            xv[c][4 * j] = t.x;
+            xv[c][4 * j + 1] = t.y;
+            xv[c][4 * j + 2] = t.z;
+            xv[c][4 * j + 3] = t.w;
           }
-          tmem_st32(tl + kColX + 32 * c, o);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(xv[c][j]);
+          tmem_st32(tl + kColX + 64 * half + 32 * c, o);
         }
         tmem_st_wait();
       }
+      pair_ln_to_smem(xv, tl, slot, half, bar_id, p.eps, p.ln1_g[0], p.ln1_b[0], sA, r);
       for (int l = 0; l < L; ++l) {
-        layer_norm_to_smem(tl + kColX, p.ln1_g[l], p.ln1_b[l], p.eps, sA, r);
-        signal();
+        signal();  // LN1 output in sA
         if (!(ok = wait_m2c())) break;
-        // QKV epilogue: bias, fp16, scatter into the attention operands.
+        // QKV epilogue: this half takes Q (or K) plus half of V.
 #pragma unroll 1
-        for (int c = 0; c < 12; ++c) {
+        for (int i = 0; i < 6; ++i) {
+          const int c = i < 4 ? 4 * half + i : 8 + 2 * half + (i - 4);
           float v[32];
           tmem_ld_row(tl + 32 * c, v);
           add_bias32(v, p.b_qkv[l] + 32 * c);
@@ -449,83 +495,104 @@ __global__ void __launch_bounds__(kThreads, 1)
           else
             store_vt32(sV, r, 32 * (c - 8), v);
         }
+        slot = 2;  // exchange slots 0, 1 were the LN1 statistics
         signal();
-        // Attention, one head at a time. P is normalised before P.V, so the
-        // attention output needs no rescaling afterwards.
+        // Attention, one head at a time; this warp owns keys [64*half, +64).
 #pragma unroll 1
         for (int h = 0; h < H; ++h) {
           if (!(ok = wait_m2c())) break;
-          float sc[4][32];
+          float sc[2][32];
           float mx = -INFINITY;
 #pragma unroll
-          for (int ch = 0; ch < 4; ++ch) {
+          for (int c = 0; c < 2; ++c) {
+            const int ch = 2 * half + c;
             if (ch >= ch_lo && ch <= ch_hi) {  // warp-uniform
-              tmem_ld_row(tl + kColS + 32 * ch, sc[ch]);
+              tmem_ld_row(tl + kColS + 32 * ch, sc[c]);
+              if (plain_tile && (!p.causal || ch < q)) {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const int key = 32 * ch + j;
-                const bool valid = key >= seq_lo && key <= key_hi;
-                sc[ch][j] = valid ? sc[ch][j] * p.scale_log2 : -INFINITY;
-                mx = fmaxf(mx, sc[ch][j]);
+                for (int j = 0; j < 32; ++j) mx = fmaxf(mx, sc[c][j]);
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                  const int key = 32 * ch + j;
+                  if (key < seq_lo || key > key_hi) sc[c][j] = -INFINITY;
+                  mx = fmaxf(mx, sc[c][j]);
+                }
               }
             }
           }
-          // A row whose keys are all padding (zero-length sequence) has
-          // mx = -inf: use 0 so every weight is exp2(-inf) = 0, never NaN.
-          if (mx == -INFINITY) mx = 0.f;
+          mx = pair_combine<true>(tl, slot++, half, bar_id, mx);
+          // All keys padding (zero-length sequence): weights exp2(-inf) = 0.
+          const float mref = (mx == -INFINITY) ? 0.f : mx * sl2;
           float sum = 0.f;
 #pragma unroll
-          for (int ch = 0; ch < 4; ++ch) {
+          for (int c = 0; c < 2; ++c) {
+            const int ch = 2 * half + c;
             if (ch >= ch_lo && ch <= ch_hi) {
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
-                sc[ch][j] = exp2f(sc[ch][j] - mx);
-                sum += sc[ch][j];
+                sc[c][j] = fast_exp2(fmaf(sc[c][j], sl2, -mref));
+                sum += sc[c][j];
               }
-            }
-          }
-          const float inv = sum > 0.f ? 1.0f / sum : 0.f;
-#pragma unroll
-          for (int ch = 0; ch < 4; ++ch) {
-            if (ch >= ch_lo && ch <= ch_hi) {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) sc[ch][j] *= inv;
             } else {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) sc[ch][j] = 0.f;
+              for (int j = 0; j < 32; ++j) sc[c][j] = 0.f;
             }
-            store_row32(sP, r, 32 * ch, sc[ch]);
+            store_row32(sP, r, 32 * ch, sc[c]);
           }
+          tmem_st1(tl + kColSum + 2 * h + half, __float_as_uint(sum));
+          tmem_st_wait();
           signal();
         }
         if (!ok || !(ok = wait_m2c())) break;  // last P.V done
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          float v[32];
-          tmem_ld_row(tl + kColO + 32 * c, v);
-          store_row32(sP, r, 32 * c, v);
+        {
+          // ctx = O / rowsum for this half's columns.
+          const int h0 = (64 * half) / HD;
+          uint32_t sums[16];
+          tmem_ld16(tl + kColSum + 2 * h0, sums);
+          tmem_ld_wait();
+          float inv[HPH];
+#pragma unroll
+          for (int k = 0; k < HPH; ++k) {
+            const float lsum = __uint_as_float(sums[2 * k]) + __uint_as_float(sums[2 * k + 1]);
+            inv[k] = lsum > 0.f ? 1.0f / lsum : 0.f;
+          }
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            float v[32];
+            tmem_ld_row(tl + kColO + 64 * half + 32 * c, v);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] *= inv[HD >= 64 ? 0 : (32 * c + j) / HD];
+            store_row32(sP, r, 64 * half + 32 * c, v);
+          }
         }
         signal();
         if (!(ok = wait_m2c())) break;  // out-proj accumulator
-        residual_add(tl + kColX, tl, p.b_out[l]);
-        layer_norm_to_smem(tl + kColX, p.ln2_g[l], p.ln2_b[l], p.eps, sP, r);
+        pair_residual_add(tl, tl, half, p.b_out[l], xv);
+        pair_ln_to_smem(xv, tl, slot, half, bar_id, p.eps, p.ln2_g[l], p.ln2_b[l], sP, r);
         signal();
         if (!(ok = wait_m2c())) break;  // FFN-in accumulator
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
+          const int col = 64 * half + 32 * c;
           float v[32];
-          tmem_ld_row(tl + kColF + 32 * c, v);
-          add_bias32(v, p.b_in[l] + 32 * c);
+          tmem_ld_row(tl + kColF + col, v);
+          add_bias32(v, p.b_in[l] + col);
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
-          store_row32(sP, r, 32 * c, v);
+          store_row32(sP, r, col, v);
         }
         signal();
         if (!(ok = wait_m2c())) break;  // FFN-out accumulator
-        residual_add(tl + kColX, tl, p.b_fo[l]);
-        if (l + 1 == L)
-          layer_norm_to_global(tl + kColX, p.lnf_g, p.lnf_b, p.eps, p.y + grow * kT,
-                               row_ok ? (row_valid ? 1 : 2) : 0);
+        pair_residual_add(tl, tl, half, p.b_fo[l], xv);
+        slot = 0;
+        if (l + 1 < L) {
+          pair_ln_to_smem(xv, tl, slot, half, bar_id, p.eps, p.ln1_g[l + 1], p.ln1_b[l + 1], sA,
+                          r);
+        } else {
+          pair_ln_to_global(xv, tl, slot, half, bar_id, p.eps, p.lnf_g, p.lnf_b,
+                            p.y + grow * kT, row_ok ? (row_valid ? 1 : 2) : 0);
+        }
       }
     }
   }
