@@ -28,16 +28,21 @@
 //   m: acc[0,384) = sA . [Wq;Wk;Wv]^T                   (three N=128 GEMMs)
 //   c: +bias -> Q into sA, K into sK, V^T into sV       (fp16)
 //   m: S = Q_h . K_h^T -> TMEM[0,128)
-//   c: masked softmax row -> P = exp2(s - max) (fp16, <= 1) into sP;
+//   c: masked softmax row -> P = exp2(s - max) (fp16, <= 1) into TMEM A;
 //      the row sum goes to TMEM
 //   m: O[128 + h*hd, +hd) = P . V_h ; S_{h+1} = ...     (per head)
-//   c: ctx = O / rowsum -> sP
+//   c: ctx = O / rowsum -> TMEM A
 //   m: acc[0,128) = ctx . Wo^T
-//   c: x += acc + bo (fp32, kept in TMEM[384,512)); LN2(x) -> sP
+//   c: x += acc + bo (fp32, kept in TMEM[384,512)); LN2(x) -> TMEM A
 //   m: acc[128,256) = h2 . W1^T
-//   c: g = gelu_erf(acc + b1) -> sP
+//   c: g = gelu_erf(acc + b1) -> TMEM A
 //   m: acc[0,128) = g . W2^T
 //   c: x += acc + b2; next layer's LN1, or final LN -> y (global, fp32)
+//
+// "TMEM A" is TMEM columns [256,320) holding a 128x128 fp16 operand (two
+// values per 32-bit column) that the next tcgen05.mma reads as its A matrix,
+// so P, ctx, h2 and g never touch shared memory. Biases and LayerNorm
+// parameters of every layer are copied to shared memory once per CTA.
 //
 // tcgen05.ld/st are warp-collective: every TMEM access of the compute warps
 // is executed by all 32 lanes; rows past the end of the batch and padded
@@ -47,7 +52,7 @@
 
 namespace tfx {
 
-constexpr int kFusedMaxLayers = 8;
+constexpr int kFusedMaxLayers = 5;
 
 struct FusedParams {
   CUtensorMap w_qkv[kFusedMaxLayers];
@@ -83,21 +88,27 @@ constexpr int kT = 128;                      // tokens per tile = d_model = ffn_
 constexpr int kOpBytes = kT * kT * 2;        // one 128x128 fp16 operand (32 KB)
 constexpr int kBlkBytes = kT * 64 * 2;       // one 128-row x 64-col SW128 block (16 KB)
 constexpr int kWSlots = 3;
+// Per-layer parameter block in shared memory (floats).
+constexpr int kPQkv = 0, kPOut = 384, kPIn = 512, kPFo = 640;
+constexpr int kPLn1g = 768, kPLn1b = 896, kPLn2g = 1024, kPLn2b = 1152;
+constexpr int kParFloats = 1280;
+constexpr int kParBytes = (kFusedMaxLayers * kParFloats + 2 * 128) * 4;
 constexpr int kOffA = 0;
 constexpr int kOffK = kOpBytes;
 constexpr int kOffV = 2 * kOpBytes;
-constexpr int kOffP = 3 * kOpBytes;
-constexpr int kOffW = 4 * kOpBytes;
-constexpr int kOffBar = kOffW + kWSlots * kOpBytes;
+constexpr int kOffW = 3 * kOpBytes;
+constexpr int kOffPar = kOffW + kWSlots * kOpBytes;
+constexpr int kOffBar = kOffPar + kParBytes;
 constexpr int kSmemBytes = kOffBar + 128 + 1024;
 constexpr int kComputeWarps = 8;
 constexpr int kThreads = 32 * (2 + kComputeWarps);
 constexpr uint32_t kColS = 0;      // attention scores (per head)
 constexpr uint32_t kColO = 128;    // attention output, all heads
 constexpr uint32_t kColF = 128;    // FFN-in accumulator
-constexpr uint32_t kColXch = 256;  // pair-exchange slots (free once the QKV
+constexpr uint32_t kColA = 256;    // fp16 A operand of the next MMA (64 cols)
+constexpr uint32_t kColXch = 320;  // pair-exchange slots (free once the QKV
                                    // epilogue has read the V accumulator)
-constexpr uint32_t kColSum = 320;  // per-head partial softmax sums
+constexpr uint32_t kColSum = 352;  // per-head partial softmax sums
 constexpr uint32_t kColX = 384;    // fp32 residual stream of the tile
 
 // Byte address of row r, columns [c, c+8) of a K-major 128x128 fp16 operand
@@ -163,11 +174,12 @@ __device__ __forceinline__ void tmem_ld_row(uint32_t taddr, float (&v)[32]) {
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
 }
 
-__device__ __forceinline__ void add_bias32(float (&v)[32], const float* __restrict__ b) {
+// v += b[0..32) (b in shared memory; every lane reads the same address).
+__device__ __forceinline__ void add_bias32(float (&v)[32], const float* b) {
   const float4* b4 = reinterpret_cast<const float4*>(b);
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    const float4 t = __ldg(b4 + j);
+    const float4 t = b4[j];
     v[4 * j] += t.x;
     v[4 * j + 1] += t.y;
     v[4 * j + 2] += t.z;
@@ -230,7 +242,7 @@ __device__ __forceinline__ void pair_ln_to_smem(const float (&x)[2][32], uint32_
     float v[32];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const float4 gg = __ldg(g4 + j), bb = __ldg(b4 + j);
+      const float4 gg = g4[j], bb = b4[j];
       v[4 * j] = (x[c][4 * j] - mean) * rstd * gg.x + bb.x;
       v[4 * j + 1] = (x[c][4 * j + 1] - mean) * rstd * gg.y + bb.y;
       v[4 * j + 2] = (x[c][4 * j + 2] - mean) * rstd * gg.z + bb.z;
@@ -238,6 +250,42 @@ __device__ __forceinline__ void pair_ln_to_smem(const float (&x)[2][32], uint32_
     }
     store_row32(base, r, col, v);
   }
+}
+
+// This warp's 64 columns of a row -> fp16 pairs in TMEM A columns
+// [32*half, +32) of this lane (the A operand of the next MMA).
+__device__ __forceinline__ void store_a_tmem(uint32_t tl, int half, const float (&v)[2][32]) {
+  uint32_t w[32];
+#pragma unroll
+  for (int c = 0; c < 2; ++c)
+#pragma unroll
+    for (int j = 0; j < 16; ++j) w[16 * c + j] = pack_half2(v[c][2 * j], v[c][2 * j + 1]);
+  tmem_st32(tl + kColA + 32 * half, w);
+  tmem_st_wait();
+}
+
+// LayerNorm of the row -> fp16 TMEM A operand (this warp's 64 columns).
+__device__ __forceinline__ void pair_ln_to_tmem(const float (&x)[2][32], uint32_t tl, int& slot,
+                                                int half, int bar_id, float eps, const float* g,
+                                                const float* b) {
+  float mean, rstd;
+  pair_row_stats(x, tl, slot, half, bar_id, eps, mean, rstd);
+  float v[2][32];
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    const int col = 64 * half + 32 * c;
+    const float4* g4 = reinterpret_cast<const float4*>(g + col);
+    const float4* b4 = reinterpret_cast<const float4*>(b + col);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 gg = g4[j], bb = b4[j];
+      v[c][4 * j] = (x[c][4 * j] - mean) * rstd * gg.x + bb.x;
+      v[c][4 * j + 1] = (x[c][4 * j + 1] - mean) * rstd * gg.y + bb.y;
+      v[c][4 * j + 2] = (x[c][4 * j + 2] - mean) * rstd * gg.z + bb.z;
+      v[c][4 * j + 3] = (x[c][4 * j + 3] - mean) * rstd * gg.w + bb.w;
+    }
+  }
+  store_a_tmem(tl, half, v);
 }
 
 // Final LayerNorm -> fp32 output columns [64*half, +64) of the row. mode:
@@ -258,7 +306,7 @@ __device__ __forceinline__ void pair_ln_to_global(const float (&x)[2][32], uint3
     float4* y4 = reinterpret_cast<float4*>(y + col);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const float4 gg = __ldg(g4 + j), bb = __ldg(b4 + j);
+      const float4 gg = g4[j], bb = b4[j];
       __stcs(y4 + j, make_float4(((x[c][4 * j] - mean) * rstd * gg.x + bb.x) * keep,
                                  ((x[c][4 * j + 1] - mean) * rstd * gg.y + bb.y) * keep,
                                  ((x[c][4 * j + 2] - mean) * rstd * gg.z + bb.z) * keep,
@@ -281,7 +329,7 @@ __device__ __forceinline__ void pair_residual_add(uint32_t tl, uint32_t t_acc, i
     const float4* b4 = reinterpret_cast<const float4*>(bias + col);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const float4 bb = __ldg(b4 + j);
+      const float4 bb = b4[j];
       x[c][4 * j] = __uint_as_float(rx[4 * j]) + (__uint_as_float(ra[4 * j]) + bb.x);
       x[c][4 * j + 1] = __uint_as_float(rx[4 * j + 1]) + (__uint_as_float(ra[4 * j + 1]) + bb.y);
       x[c][4 * j + 2] = __uint_as_float(rx[4 * j + 2]) + (__uint_as_float(ra[4 * j + 2]) + bb.z);
@@ -302,7 +350,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
-  const uint32_t sA = sbase + kOffA, sK = sbase + kOffK, sV = sbase + kOffV, sP = sbase + kOffP;
+  const uint32_t sA = sbase + kOffA, sK = sbase + kOffK, sV = sbase + kOffV;
+  float* par = reinterpret_cast<float*>(smem + kOffPar);  // [layer][kParFloats], then final LN
   uint64_t* w_full = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* w_empty = w_full + kWSlots;
   uint64_t* c2m = w_empty + kWSlots;  // compute -> MMA hand-off (one arrival per compute warp)
@@ -323,11 +372,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
+  const int L = p.num_layers;
+  // Biases and LayerNorm parameters of every layer -> shared memory, once.
+  for (int i = threadIdx.x; i < L * kParFloats + 256; i += kThreads) {
+    float v;
+    if (i >= L * kParFloats) {
+      const int j = i - L * kParFloats;
+      v = j < 128 ? p.lnf_g[j] : p.lnf_b[j - 128];
+      par[kFusedMaxLayers * kParFloats + j] = v;
+      continue;
+    }
+    const int l = i / kParFloats, j = i % kParFloats;
+    if (j < kPOut) v = p.b_qkv[l][j];
+    else if (j < kPIn) v = p.b_out[l][j - kPOut];
+    else if (j < kPFo) v = p.b_in[l][j - kPIn];
+    else if (j < kPLn1g) v = p.b_fo[l][j - kPFo];
+    else if (j < kPLn1b) v = p.ln1_g[l][j - kPLn1g];
+    else if (j < kPLn2g) v = p.ln1_b[l][j - kPLn1b];
+    else if (j < kPLn2b) v = p.ln2_g[l][j - kPLn2g];
+    else v = p.ln2_b[l][j - kPLn2b];
+    par[i] = v;
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int L = p.num_layers;
+  const float* parf = par + kFusedMaxLayers * kParFloats;  // final LN gamma | beta
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------- weight producer
@@ -373,11 +443,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       return r;
     };
+    // D = A . W^T with W the next ring slot; A in smem (a != 0) or, when
+    // a == 0, the fp16 operand in TMEM A columns.
     auto gemm_w = [&](uint32_t dcol, uint32_t a) {
       if (!mbar_wait(&w_full[slot], ph, p.err, kDevTimeoutFull)) return false;
       tc_fence_after();
       const uint32_t w = sbase + kOffW + static_cast<uint32_t>(slot * kOpBytes);
-      mma_chain(tmem + dcol, a, 0, w, 0, kT / 16, id128);
+      if (a != 0) {
+        mma_chain(tmem + dcol, a, 0, w, 0, kT / 16, id128);
+      } else {
+        for (int k = 0; k < kT / 16; ++k)
+          mma_f16_ts(tmem + dcol, tmem + kColA + 8 * k, op_desc(w, 16 * k), id128,
+                     k > 0 ? 1u : 0u);
+      }
       mma_commit(&w_empty[slot]);
       if (++slot == kWSlots) {
         slot = 0;
@@ -396,23 +474,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_chain(tmem + kColS, sA, 0, sK, 0, HD / 16, id128);
         mma_commit(m2c);
         for (int h = 0; h < H && ok; ++h) {
-          if (!(ok = wait_c2m())) break;  // P_h in sP
+          if (!(ok = wait_c2m())) break;  // P_h in TMEM A
           for (int k = 0; k < kT / 16; ++k)
-            mma_f16_ss(tmem + kColO + h * HD, op_desc(sP, 16 * k),
+            mma_f16_ts(tmem + kColO + h * HD, tmem + kColA + 8 * k,
                        op_desc(sV + static_cast<uint32_t>(h * HD * 128), 16 * k), idhd,
                        k > 0 ? 1u : 0u);
           if (h + 1 < H)
             mma_chain(tmem + kColS, sA, (h + 1) * HD, sK, (h + 1) * HD, HD / 16, id128);
           mma_commit(m2c);
         }
-        if (!ok || !(ok = wait_c2m())) break;  // ctx in sP
-        if (!(ok = gemm_w(0, sP))) break;
+        if (!ok || !(ok = wait_c2m())) break;  // ctx in TMEM A
+        if (!(ok = gemm_w(0, 0))) break;
         mma_commit(m2c);
-        if (!(ok = wait_c2m())) break;  // LN2 output in sP
-        if (!(ok = gemm_w(kColF, sP))) break;
+        if (!(ok = wait_c2m())) break;  // LN2 output in TMEM A
+        if (!(ok = gemm_w(kColF, 0))) break;
         mma_commit(m2c);
-        if (!(ok = wait_c2m())) break;  // GELU output in sP
-        if (!(ok = gemm_w(0, sP))) break;
+        if (!(ok = wait_c2m())) break;  // GELU output in TMEM A
+        if (!(ok = gemm_w(0, 0))) break;
         mma_commit(m2c);
       }
     }
@@ -477,8 +555,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tmem_st_wait();
       }
-      pair_ln_to_smem(xv, tl, slot, half, bar_id, p.eps, p.ln1_g[0], p.ln1_b[0], sA, r);
+      pair_ln_to_smem(xv, tl, slot, half, bar_id, p.eps, par + kPLn1g, par + kPLn1b, sA, r);
       for (int l = 0; l < L; ++l) {
+        const float* lp = par + l * kParFloats;
         signal();  // LN1 output in sA
         if (!(ok = wait_m2c())) break;
         // QKV epilogue: this half takes Q (or K) plus half of V.
@@ -487,7 +566,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int c = i < 4 ? 4 * half + i : 8 + 2 * half + (i - 4);
           float v[32];
           tmem_ld_row(tl + 32 * c, v);
-          add_bias32(v, p.b_qkv[l] + 32 * c);
+          add_bias32(v, lp + kPQkv + 32 * c);
           if (c < 4)
             store_row32(sA, r, 32 * c, v);
           else if (c < 8)
@@ -538,10 +617,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int j = 0; j < 32; ++j) sc[c][j] = 0.f;
             }
-            store_row32(sP, r, 32 * ch, sc[c]);
           }
           tmem_st1(tl + kColSum + 2 * h + half, __float_as_uint(sum));
-          tmem_st_wait();
+          store_a_tmem(tl, half, sc);
           signal();
         }
         if (!ok || !(ok = wait_m2c())) break;  // last P.V done
@@ -557,40 +635,42 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float lsum = __uint_as_float(sums[2 * k]) + __uint_as_float(sums[2 * k + 1]);
             inv[k] = lsum > 0.f ? 1.0f / lsum : 0.f;
           }
+          float v[2][32];
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
-            float v[32];
-            tmem_ld_row(tl + kColO + 64 * half + 32 * c, v);
+            tmem_ld_row(tl + kColO + 64 * half + 32 * c, v[c]);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] *= inv[HD >= 64 ? 0 : (32 * c + j) / HD];
-            store_row32(sP, r, 64 * half + 32 * c, v);
+            for (int j = 0; j < 32; ++j) v[c][j] *= inv[HD >= 64 ? 0 : (32 * c + j) / HD];
           }
+          store_a_tmem(tl, half, v);
         }
         signal();
         if (!(ok = wait_m2c())) break;  // out-proj accumulator
-        pair_residual_add(tl, tl, half, p.b_out[l], xv);
-        pair_ln_to_smem(xv, tl, slot, half, bar_id, p.eps, p.ln2_g[l], p.ln2_b[l], sP, r);
+        pair_residual_add(tl, tl, half, lp + kPOut, xv);
+        pair_ln_to_tmem(xv, tl, slot, half, bar_id, p.eps, lp + kPLn2g, lp + kPLn2b);
         signal();
         if (!(ok = wait_m2c())) break;  // FFN-in accumulator
+        {
+          float v[2][32];
 #pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-          const int col = 64 * half + 32 * c;
-          float v[32];
-          tmem_ld_row(tl + kColF + col, v);
-          add_bias32(v, p.b_in[l] + col);
+          for (int c = 0; c < 2; ++c) {
+            const int col = 64 * half + 32 * c;
+            tmem_ld_row(tl + kColF + col, v[c]);
+            add_bias32(v[c], lp + kPIn + col);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
-          store_row32(sP, r, col, v);
+            for (int j = 0; j < 32; ++j) v[c][j] = gelu_erf(v[c][j]);
+          }
+          store_a_tmem(tl, half, v);
         }
         signal();
         if (!(ok = wait_m2c())) break;  // FFN-out accumulator
-        pair_residual_add(tl, tl, half, p.b_fo[l], xv);
+        pair_residual_add(tl, tl, half, lp + kPFo, xv);
         slot = 0;
         if (l + 1 < L) {
-          pair_ln_to_smem(xv, tl, slot, half, bar_id, p.eps, p.ln1_g[l + 1], p.ln1_b[l + 1], sA,
-                          r);
+          pair_ln_to_smem(xv, tl, slot, half, bar_id, p.eps, lp + kParFloats + kPLn1g,
+                          lp + kParFloats + kPLn1b, sA, r);
         } else {
-          pair_ln_to_global(xv, tl, slot, half, bar_id, p.eps, p.lnf_g, p.lnf_b,
+          pair_ln_to_global(xv, tl, slot, half, bar_id, p.eps, parf, parf + 128,
                             p.y + grow * kT, row_ok ? (row_valid ? 1 : 2) : 0);
         }
       }
