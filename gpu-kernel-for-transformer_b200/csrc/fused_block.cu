@@ -374,25 +374,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   const int L = p.num_layers;
   // Biases and LayerNorm parameters of every layer -> shared memory, once.
-  for (int i = threadIdx.x; i < L * kParFloats + 256; i += kThreads) {
-    float v;
-    if (i >= L * kParFloats) {
-      const int j = i - L * kParFloats;
-      v = j < 128 ? p.lnf_g[j] : p.lnf_b[j - 128];
-      par[kFusedMaxLayers * kParFloats + j] = v;
-      continue;
+#pragma unroll
+  for (int l = 0; l < kFusedMaxLayers; ++l) {  // static indices into the param arrays
+    if (l < L) {
+      float* dst = par + l * kParFloats;
+      for (int j = threadIdx.x; j < kParFloats; j += kThreads) {
+        float v;
+        if (j < kPOut) v = p.b_qkv[l][j];
+        else if (j < kPIn) v = p.b_out[l][j - kPOut];
+        else if (j < kPFo) v = p.b_in[l][j - kPIn];
+        else if (j < kPLn1g) v = p.b_fo[l][j - kPFo];
+        else if (j < kPLn1b) v = p.ln1_g[l][j - kPLn1g];
+        else if (j < kPLn2g) v = p.ln1_b[l][j - kPLn1b];
+        else if (j < kPLn2b) v = p.ln2_g[l][j - kPLn2g];
+        else v = p.ln2_b[l][j - kPLn2b];
+        dst[j] = v;
+      }
     }
-    const int l = i / kParFloats, j = i % kParFloats;
-    if (j < kPOut) v = p.b_qkv[l][j];
-    else if (j < kPIn) v = p.b_out[l][j - kPOut];
-    else if (j < kPFo) v = p.b_in[l][j - kPIn];
-    else if (j < kPLn1g) v = p.b_fo[l][j - kPFo];
-    else if (j < kPLn1b) v = p.ln1_g[l][j - kPLn1g];
-    else if (j < kPLn2g) v = p.ln1_b[l][j - kPLn1b];
-    else if (j < kPLn2b) v = p.ln2_g[l][j - kPLn2g];
-    else v = p.ln2_b[l][j - kPLn2b];
-    par[i] = v;
   }
+  for (int j = threadIdx.x; j < 256; j += kThreads)
+    par[kFusedMaxLayers * kParFloats + j] = j < 128 ? p.lnf_g[j] : p.lnf_b[j - 128];
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -580,22 +581,24 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
         for (int h = 0; h < H; ++h) {
           if (!(ok = wait_m2c())) break;
-          float sc[2][32];
+          // Two passes over this warp's (at most two) 32-key chunks so only
+          // one chunk is live in registers: masked row max, then exp2 + sum
+          // + fp16 packing into the TMEM A operand.
           float mx = -INFINITY;
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             const int ch = 2 * half + c;
             if (ch >= ch_lo && ch <= ch_hi) {  // warp-uniform
-              tmem_ld_row(tl + kColS + 32 * ch, sc[c]);
+              float sc[32];
+              tmem_ld_row(tl + kColS + 32 * ch, sc);
               if (plain_tile && (!p.causal || ch < q)) {
 #pragma unroll
-                for (int j = 0; j < 32; ++j) mx = fmaxf(mx, sc[c][j]);
+                for (int j = 0; j < 32; ++j) mx = fmaxf(mx, sc[j]);
               } else {
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
                   const int key = 32 * ch + j;
-                  if (key < seq_lo || key > key_hi) sc[c][j] = -INFINITY;
-                  mx = fmaxf(mx, sc[c][j]);
+                  if (key >= seq_lo && key <= key_hi) mx = fmaxf(mx, sc[j]);
                 }
               }
             }
@@ -604,22 +607,32 @@ __global__ void __launch_bounds__(kThreads, 1)
           // All keys padding (zero-length sequence): weights exp2(-inf) = 0.
           const float mref = (mx == -INFINITY) ? 0.f : mx * sl2;
           float sum = 0.f;
+          uint32_t w[32];
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             const int ch = 2 * half + c;
             if (ch >= ch_lo && ch <= ch_hi) {
+              float sc[32];
+              tmem_ld_row(tl + kColS + 32 * ch, sc);
+              const bool plain = plain_tile && (!p.causal || ch < q);
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
-                sc[c][j] = fast_exp2(fmaf(sc[c][j], sl2, -mref));
-                sum += sc[c][j];
+                const int key = 32 * ch + j;
+                float e = fast_exp2(fmaf(sc[j], sl2, -mref));
+                if (!plain && (key < seq_lo || key > key_hi)) e = 0.f;
+                sc[j] = e;
+                sum += e;
               }
+#pragma unroll
+              for (int j = 0; j < 16; ++j) w[16 * c + j] = pack_half2(sc[2 * j], sc[2 * j + 1]);
             } else {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) sc[c][j] = 0.f;
+              for (int j = 0; j < 16; ++j) w[16 * c + j] = 0u;
             }
           }
           tmem_st1(tl + kColSum + 2 * h + half, __float_as_uint(sum));
-          store_a_tmem(tl, half, sc);
+          tmem_st32(tl + kColA + 32 * half, w);
+          tmem_st_wait();
           signal();
         }
         if (!ok || !(ok = wait_m2c())) break;  // last P.V done
