@@ -8,41 +8,36 @@
 // with every intermediate on chip: HBM sees the fp32 input once and the fp32
 // output once (1 KB per token), instead of ~27 KB per token for the chain of
 // separate kernels. Weights (192 KB fp16 per layer) stream from L2 through a
-// TMA ring.
+// TMA ring; biases and LayerNorm parameters sit in shared memory.
 //
 // Roles (320 threads):
 //   warp 0      TMA producer: per layer Wq, Wk, Wv, Wo, W1, W2 (128x128 fp16
 //               each, 128-byte swizzle) into a 3-slot ring
 //   warp 1      TMEM owner (all 512 columns) + single-thread tcgen05.mma issuer
 //   warps 2..9  compute, two warps per TMEM lane quarter: lane l of warp w
-//               owns token row 32*(w%4)+l of the tile and HALF of its columns
-//               (half = (w-2)/4: columns / keys [64*half, 64*half+64)), and
-//               does every row-wise step (LayerNorms, bias, GELU, softmax,
-//               residual adds) straight out of TMEM. Row reductions (LN
-//               statistics, softmax max) are combined with the partner warp
-//               through free TMEM columns and a 64-thread named barrier.
+//               owns row 32*(w%4)+l of every 128-row accumulator and HALF of
+//               its columns (half = (w-2)/4). Row statistics (LayerNorm mean /
+//               variance, softmax max, softmax sums) are merged with the
+//               partner warp through shared memory and a 64-thread barrier.
 //
-// Per layer (c = compute warps, m = MMA thread; each step is an mbarrier
-// hand-off to the other side):
-//   c: LN1(x) -> sA                                     (fp16, K-major SW128)
-//   m: acc[0,384) = sA . [Wq;Wk;Wv]^T                   (three N=128 GEMMs)
-//   c: +bias -> Q into sA, K into sK, V^T into sV       (fp16)
-//   m: S = Q_h . K_h^T -> TMEM[0,128)
-//   c: masked softmax row -> P = exp2(s - max) (fp16, <= 1) into TMEM A;
-//      the row sum goes to TMEM
-//   m: O[128 + h*hd, +hd) = P . V_h ; S_{h+1} = ...     (per head)
-//   c: ctx = O / rowsum -> TMEM A
-//   m: acc[0,128) = ctx . Wo^T
-//   c: x += acc + bo (fp32, kept in TMEM[384,512)); LN2(x) -> TMEM A
-//   m: acc[128,256) = h2 . W1^T
-//   c: g = gelu_erf(acc + b1) -> TMEM A
-//   m: acc[0,128) = g . W2^T
-//   c: x += acc + b2; next layer's LN1, or final LN -> y (global, fp32)
+// TMEM columns: [0,128) S buffer 0 / Q / out-proj and FFN-out accumulators;
+// [128,256) S buffer 1 / K / FFN-in accumulator; [256,384) V^T accumulator,
+// then the per-head attention outputs O (two buffers), then the fp16 A operand
+// of the FFN GEMMs; [384,512) the fp32 residual stream x of the tile.
 //
-// "TMEM A" is TMEM columns [256,320) holding a 128x128 fp16 operand (two
-// values per 32-bit column) that the next tcgen05.mma reads as its A matrix,
-// so P, ctx, h2 and g never touch shared memory. Biases and LayerNorm
-// parameters of every layer are copied to shared memory once per CTA.
+// Per layer (c = compute warps, m = MMA thread):
+//   c: LN1(x) -> sA (fp16, K-major, 128B swizzle)
+//   m: Q = h.Wq^T, K = h.Wk^T, V^T = Wv.h^T (V^T computed transposed so it is
+//      already the K-major B operand of P.V)
+//   c: + biases -> Q into sA, K into sK, V^T into sV
+//   m: S_0 -> S buffer 0, S_1 -> S buffer 1
+//   per head h (b = h % 2):
+//     c: softmax row of S_h -> P_h (fp16, <= 1) written over its own S buffer
+//     m: O_h = P_h . V_h -> O buffer b ; S_{h+2} -> S buffer b
+//     c: (while the MMAs run) ctx_{h-1} = O_{h-1} / rowsum -> sA over Q_{h-1}
+//   m: acc = ctx . Wo^T        c: x += acc + bo; LN2(x) -> TMEM A operand
+//   m: acc = h2 . W1^T         c: g = gelu(acc + b1) -> TMEM A operand
+//   m: acc = g . W2^T          c: x += acc + b2; next LN1 or final LN -> y
 //
 // tcgen05.ld/st are warp-collective: every TMEM access of the compute warps
 // is executed by all 32 lanes; rows past the end of the batch and padded
@@ -93,23 +88,27 @@ constexpr int kPQkv = 0, kPOut = 384, kPIn = 512, kPFo = 640;
 constexpr int kPLn1g = 768, kPLn1b = 896, kPLn2g = 1024, kPLn2b = 1152;
 constexpr int kParFloats = 1280;
 constexpr int kParBytes = (kFusedMaxLayers * kParFloats + 2 * 128) * 4;
+constexpr int kXchSlots = 2;                              // alternating pair-exchange slots
+constexpr int kXchBytes = kXchSlots * 2 * kT * 8;         // [slot][half][row] float2
+constexpr int kSumBytes = 2 * 2 * kT * 4;                 // [head parity][half][row] float
 constexpr int kOffA = 0;
 constexpr int kOffK = kOpBytes;
 constexpr int kOffV = 2 * kOpBytes;
 constexpr int kOffW = 3 * kOpBytes;
 constexpr int kOffPar = kOffW + kWSlots * kOpBytes;
-constexpr int kOffBar = kOffPar + kParBytes;
+constexpr int kOffXch = kOffPar + kParBytes;
+constexpr int kOffSum = kOffXch + kXchBytes;
+constexpr int kOffBar = kOffSum + kSumBytes;
 constexpr int kSmemBytes = kOffBar + 128 + 1024;
 constexpr int kComputeWarps = 8;
 constexpr int kThreads = 32 * (2 + kComputeWarps);
-constexpr uint32_t kColS = 0;      // attention scores (per head)
-constexpr uint32_t kColO = 128;    // attention output, all heads
-constexpr uint32_t kColF = 128;    // FFN-in accumulator
-constexpr uint32_t kColA = 256;    // fp16 A operand of the next MMA (64 cols)
-constexpr uint32_t kColXch = 320;  // pair-exchange slots (free once the QKV
-                                   // epilogue has read the V accumulator)
-constexpr uint32_t kColSum = 352;  // per-head partial softmax sums
-constexpr uint32_t kColX = 384;    // fp32 residual stream of the tile
+constexpr uint32_t kColS0 = 0;    // S buffer 0 (P_h aliased into it)
+constexpr uint32_t kColS1 = 128;  // S buffer 1
+constexpr uint32_t kColO = 256;   // attention output buffers (2 x head_dim columns)
+constexpr uint32_t kColF = 128;   // FFN-in accumulator
+constexpr uint32_t kColA = 256;   // fp16 A operand of the FFN GEMMs (64 columns)
+constexpr uint32_t kColX = 384;   // fp32 residual stream of the tile
+static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 // Byte address of row r, columns [c, c+8) of a K-major 128x128 fp16 operand
 // stored as two 128B-swizzled 64-column blocks (the layout TMA writes with
@@ -126,30 +125,14 @@ __device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, ui
                : "memory");
 }
 
-__device__ __forceinline__ void sts16(uint32_t addr, __half v) {
-  asm volatile("st.shared.b16 [%0], %1;" ::"r"(addr), "h"(__half_as_ushort(v)) : "memory");
-}
-
-// Row r, columns [c0, c0+32) of a K-major operand <- fp16(v).
-__device__ __forceinline__ void store_row32(uint32_t base, int r, int c0, const float* v) {
+// Row r, columns [c0, c0 + 8*N8) of a K-major operand <- fp16(v).
+template <int N8>
+__device__ __forceinline__ void store_row(uint32_t base, int r, int c0, const float* v) {
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
+  for (int j = 0; j < N8; ++j) {
     sts128(sw_addr(base, r, c0 + 8 * j), pack_half2(v[8 * j], v[8 * j + 1]),
            pack_half2(v[8 * j + 2], v[8 * j + 3]), pack_half2(v[8 * j + 4], v[8 * j + 5]),
            pack_half2(v[8 * j + 6], v[8 * j + 7]));
-  }
-}
-
-// V^T operand (rows = feature d, columns = key): write key row `key`,
-// features [d0, d0+32).
-__device__ __forceinline__ void store_vt32(uint32_t base, int key, int d0, const float* v) {
-  const uint32_t kb = static_cast<uint32_t>((key >> 6) * kBlkBytes + ((key & 7) << 1));
-  const int kc = (key & 63) >> 3;
-#pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    const int d = d0 + j;
-    sts16(base + kb + static_cast<uint32_t>(d * 128 + ((kc ^ (d & 7)) << 4)),
-          __float2half_rn(v[j]));
   }
 }
 
@@ -158,7 +141,7 @@ __device__ __forceinline__ uint64_t op_desc(uint32_t base, int col) {
 }
 
 // D[128 x N] (+)= A[128 x K] . B[N x K]^T over k-steps of 16 starting at K
-// offsets a_col/b_col.
+// offsets a_col/b_col (both operands K-major in shared memory).
 __device__ __forceinline__ void mma_chain(uint32_t d, uint32_t a, int a_col, uint32_t b,
                                           int b_col, int ksteps, uint32_t idesc) {
   for (int k = 0; k < ksteps; ++k)
@@ -187,68 +170,68 @@ __device__ __forceinline__ void add_bias32(float (&v)[32], const float* b) {
   }
 }
 
-// Per-row partial (sum or max) of this warp combined with the partner warp
-// that owns the other half of the same rows: written to TMEM column
-// kColXch + 2*slot + half, read back from the partner's column after a
-// 64-thread named barrier. Both warps get the identical result.
-template <bool IS_MAX>
-__device__ __forceinline__ float pair_combine(uint32_t tl, int slot, int half, int bar_id,
-                                              float mine) {
-  tmem_st1(tl + kColXch + 2 * slot + half, __float_as_uint(mine));
-  tmem_st_wait();
-  tc_fence_before();
-  named_bar_sync(bar_id, 64);
-  tc_fence_after();
-  uint32_t o;
-  tmem_ld1(tl + kColXch + 2 * slot + (half ^ 1), o);
-  tmem_ld_wait();
-  const float other = __uint_as_float(o);
-  return IS_MAX ? fmaxf(mine, other) : mine + other;
-}
+// The two warps of a lane quarter ("pair") exchange one float2 per row
+// through shared memory. Two slots alternate: slot k%2 is rewritten by
+// exchange k+2 only after the writer passed the barrier of exchange k+1,
+// which the partner reaches only after reading exchange k.
+struct Pair {
+  float2* xch;  // [kXchSlots][2][128]
+  int half, r, bar_id, slot;
+  __device__ __forceinline__ float2 swap(float2 mine) {
+    float2* s = xch + slot * 2 * kT;
+    slot = (slot + 1) & (kXchSlots - 1);
+    s[half * kT + r] = mine;
+    named_bar_sync(bar_id, 64);
+    return s[(half ^ 1) * kT + r];
+  }
+};
 
-// Mean and rstd of the full 128-wide row from this warp's 64 values.
-__device__ __forceinline__ void pair_row_stats(const float (&x)[2][32], uint32_t tl, int& slot,
-                                               int half, int bar_id, float eps, float& mean,
-                                               float& rstd) {
+// Mean and rstd of the full 128-wide row from this warp's 64 values: local
+// mean and centred sum of squares per half, merged with Chan et al.'s
+// parallel formula (M2 = M2a + M2b + d^2 * na*nb/n). Both warps compute the
+// same numbers in the same order.
+__device__ __forceinline__ void row_stats(const float (&x)[2][32], Pair& pr, float eps,
+                                          float& mean, float& rstd) {
   float s = 0.f;
 #pragma unroll
   for (int c = 0; c < 2; ++c)
 #pragma unroll
     for (int j = 0; j < 32; ++j) s += x[c][j];
-  mean = pair_combine<false>(tl, slot++, half, bar_id, s) * (1.0f / 128.0f);
+  const float m_half = s * (1.0f / 64.0f);
   float q = 0.f;
 #pragma unroll
   for (int c = 0; c < 2; ++c)
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
-      const float t = x[c][j] - mean;
+      const float t = x[c][j] - m_half;
       q = fmaf(t, t, q);
     }
-  rstd = rsqrtf(pair_combine<false>(tl, slot++, half, bar_id, q) * (1.0f / 128.0f) + eps);
+  const float2 o = pr.swap(make_float2(m_half, q));
+  const float m0 = pr.half == 0 ? m_half : o.x, m1 = pr.half == 0 ? o.x : m_half;
+  const float q0 = pr.half == 0 ? q : o.y, q1 = pr.half == 0 ? o.y : q;
+  mean = 0.5f * (m0 + m1);
+  const float d = m1 - m0;
+  const float m2 = (q0 + q1) + d * d * 32.0f;
+  rstd = rsqrtf(m2 * (1.0f / 128.0f) + eps);
 }
 
-// LayerNorm of the row (this warp's half in registers) -> fp16 columns
-// [64*half, +64) of row r of K-major operand `base`.
-__device__ __forceinline__ void pair_ln_to_smem(const float (&x)[2][32], uint32_t tl, int& slot,
-                                                int half, int bar_id, float eps, const float* g,
-                                                const float* b, uint32_t base, int r) {
-  float mean, rstd;
-  pair_row_stats(x, tl, slot, half, bar_id, eps, mean, rstd);
+// Normalised + affine values of this warp's 64 columns.
+__device__ __forceinline__ void ln_apply(const float (&x)[2][32], float mean, float rstd,
+                                         const float* g, const float* b, int half,
+                                         float (&v)[2][32]) {
 #pragma unroll
   for (int c = 0; c < 2; ++c) {
     const int col = 64 * half + 32 * c;
     const float4* g4 = reinterpret_cast<const float4*>(g + col);
     const float4* b4 = reinterpret_cast<const float4*>(b + col);
-    float v[32];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const float4 gg = g4[j], bb = b4[j];
-      v[4 * j] = (x[c][4 * j] - mean) * rstd * gg.x + bb.x;
-      v[4 * j + 1] = (x[c][4 * j + 1] - mean) * rstd * gg.y + bb.y;
-      v[4 * j + 2] = (x[c][4 * j + 2] - mean) * rstd * gg.z + bb.z;
-      v[4 * j + 3] = (x[c][4 * j + 3] - mean) * rstd * gg.w + bb.w;
+      v[c][4 * j] = (x[c][4 * j] - mean) * rstd * gg.x + bb.x;
+      v[c][4 * j + 1] = (x[c][4 * j + 1] - mean) * rstd * gg.y + bb.y;
+      v[c][4 * j + 2] = (x[c][4 * j + 2] - mean) * rstd * gg.z + bb.z;
+      v[c][4 * j + 3] = (x[c][4 * j + 3] - mean) * rstd * gg.w + bb.w;
     }
-    store_row32(base, r, col, v);
   }
 }
 
@@ -264,61 +247,10 @@ __device__ __forceinline__ void store_a_tmem(uint32_t tl, int half, const float 
   tmem_st_wait();
 }
 
-// LayerNorm of the row -> fp16 TMEM A operand (this warp's 64 columns).
-__device__ __forceinline__ void pair_ln_to_tmem(const float (&x)[2][32], uint32_t tl, int& slot,
-                                                int half, int bar_id, float eps, const float* g,
-                                                const float* b) {
-  float mean, rstd;
-  pair_row_stats(x, tl, slot, half, bar_id, eps, mean, rstd);
-  float v[2][32];
-#pragma unroll
-  for (int c = 0; c < 2; ++c) {
-    const int col = 64 * half + 32 * c;
-    const float4* g4 = reinterpret_cast<const float4*>(g + col);
-    const float4* b4 = reinterpret_cast<const float4*>(b + col);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float4 gg = g4[j], bb = b4[j];
-      v[c][4 * j] = (x[c][4 * j] - mean) * rstd * gg.x + bb.x;
-      v[c][4 * j + 1] = (x[c][4 * j + 1] - mean) * rstd * gg.y + bb.y;
-      v[c][4 * j + 2] = (x[c][4 * j + 2] - mean) * rstd * gg.z + bb.z;
-      v[c][4 * j + 3] = (x[c][4 * j + 3] - mean) * rstd * gg.w + bb.w;
-    }
-  }
-  store_a_tmem(tl, half, v);
-}
-
-// Final LayerNorm -> fp32 output columns [64*half, +64) of the row. mode:
-// 0 = store nothing (row past the batch), 1 = the row, 2 = zeros (padded token).
-__device__ __forceinline__ void pair_ln_to_global(const float (&x)[2][32], uint32_t tl, int& slot,
-                                                  int half, int bar_id, float eps, const float* g,
-                                                  const float* b, float* __restrict__ y,
-                                                  int mode) {
-  float mean, rstd;
-  pair_row_stats(x, tl, slot, half, bar_id, eps, mean, rstd);
-  if (mode == 0) return;
-  const float keep = mode == 1 ? 1.0f : 0.0f;
-#pragma unroll
-  for (int c = 0; c < 2; ++c) {
-    const int col = 64 * half + 32 * c;
-    const float4* g4 = reinterpret_cast<const float4*>(g + col);
-    const float4* b4 = reinterpret_cast<const float4*>(b + col);
-    float4* y4 = reinterpret_cast<float4*>(y + col);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float4 gg = g4[j], bb = b4[j];
-      __stcs(y4 + j, make_float4(((x[c][4 * j] - mean) * rstd * gg.x + bb.x) * keep,
-                                 ((x[c][4 * j + 1] - mean) * rstd * gg.y + bb.y) * keep,
-                                 ((x[c][4 * j + 2] - mean) * rstd * gg.z + bb.z) * keep,
-                                 ((x[c][4 * j + 3] - mean) * rstd * gg.w + bb.w) * keep));
-    }
-  }
-}
-
 // x[TMEM, this warp's half] += acc + bias; the new values are also returned
 // in registers for the LayerNorm that always follows.
-__device__ __forceinline__ void pair_residual_add(uint32_t tl, uint32_t t_acc, int half,
-                                                  const float* bias, float (&x)[2][32]) {
+__device__ __forceinline__ void residual_add(uint32_t tl, uint32_t t_acc, int half,
+                                             const float* bias, float (&x)[2][32]) {
 #pragma unroll
   for (int c = 0; c < 2; ++c) {
     const int col = 64 * half + 32 * c;
@@ -352,11 +284,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t sbase = smem_u32(smem);
   const uint32_t sA = sbase + kOffA, sK = sbase + kOffK, sV = sbase + kOffV;
   float* par = reinterpret_cast<float*>(smem + kOffPar);  // [layer][kParFloats], then final LN
+  float2* xch = reinterpret_cast<float2*>(smem + kOffXch);
+  float* psum = reinterpret_cast<float*>(smem + kOffSum);  // [head parity][half][row]
   uint64_t* w_full = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* w_empty = w_full + kWSlots;
-  uint64_t* c2m = w_empty + kWSlots;  // compute -> MMA hand-off (one arrival per compute warp)
-  uint64_t* m2c = c2m + 1;            // MMA -> compute hand-off (tcgen05.commit)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(m2c + 1);
+  uint64_t* c2m = w_empty + kWSlots;  // compute -> MMA: operand ready (one arrival per warp)
+  uint64_t* m2c_g = c2m + 1;          // MMA -> compute: GEMM accumulator ready
+  uint64_t* m2c_s = m2c_g + 1;        // [2] MMA -> compute: S buffer b ready
+  uint64_t* m2c_o = m2c_s + 2;        // [2] MMA -> compute: O buffer b ready
+  // [2] compute -> MMA: P_h written into S buffer b. Separate from c2m: with
+  // two S buffers in flight a lightly loaded warp may finish head h+1 before
+  // a heavy warp finishes head h, so one barrier would let phases run ahead.
+  uint64_t* c2m_p = m2c_o + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(c2m_p + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -365,7 +305,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&w_empty[s], 1);
     }
     mbar_init(c2m, kComputeWarps);
-    mbar_init(m2c, 1);
+    mbar_init(m2c_g, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&m2c_s[b], 1);
+      mbar_init(&m2c_o[b], 1);
+      mbar_init(&c2m_p[b], kComputeWarps);
+    }
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -438,76 +383,106 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr uint32_t idhd = idesc_f16_f32(128, HD);
     int slot = 0;
     uint32_t ph = 0, c2m_ph = 0;
+    uint32_t mph_o[2] = {0, 0};  // this thread's view of the O-buffer barriers
+    uint32_t mph_p[2] = {0, 0};  // ... and of the P-ready barriers
     auto wait_c2m = [&]() {
       const bool r = mbar_wait(c2m, c2m_ph, p.err, kDevTimeoutOther);
       c2m_ph ^= 1;
       tc_fence_after();
       return r;
     };
-    // D = A . W^T with W the next ring slot; A in smem (a != 0) or, when
-    // a == 0, the fp16 operand in TMEM A columns.
-    auto gemm_w = [&](uint32_t dcol, uint32_t a) {
+    auto take_w = [&](uint32_t& w) {
       if (!mbar_wait(&w_full[slot], ph, p.err, kDevTimeoutFull)) return false;
       tc_fence_after();
-      const uint32_t w = sbase + kOffW + static_cast<uint32_t>(slot * kOpBytes);
-      if (a != 0) {
-        mma_chain(tmem + dcol, a, 0, w, 0, kT / 16, id128);
-      } else {
-        for (int k = 0; k < kT / 16; ++k)
-          mma_f16_ts(tmem + dcol, tmem + kColA + 8 * k, op_desc(w, 16 * k), id128,
-                     k > 0 ? 1u : 0u);
-      }
+      w = sbase + kOffW + static_cast<uint32_t>(slot * kOpBytes);
+      return true;
+    };
+    auto release_w = [&]() {
       mma_commit(&w_empty[slot]);
       if (++slot == kWSlots) {
         slot = 0;
         ph ^= 1;
       }
+    };
+    // D = A . W^T, A the fp16 operand in TMEM A columns.
+    auto gemm_tmem_a = [&](uint32_t dcol) {
+      uint32_t w;
+      if (!take_w(w)) return false;
+      for (int k = 0; k < kT / 16; ++k)
+        mma_f16_ts(tmem + dcol, tmem + kColA + 8 * k, op_desc(w, 16 * k), id128, k > 0 ? 1u : 0u);
+      release_w();
       return true;
+    };
+    auto issue_s = [&](int h) {  // S_h = Q_h . K_h^T -> S buffer h % 2
+      mma_chain(tmem + ((h & 1) ? kColS1 : kColS0), sA, h * HD, sK, h * HD, HD / 16, id128);
+      mma_commit(&m2c_s[h & 1]);
     };
     bool ok = true;
     for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
       for (int l = 0; l < L && ok; ++l) {
-        ok = wait_c2m();  // LN1 output in sA
-        for (int c = 0; c < 3 && ok; ++c) ok = gemm_w(kT * c, sA);
-        if (!ok) break;
-        mma_commit(m2c);
+        uint32_t w;
+        if (!(ok = wait_c2m())) break;  // LN1 output in sA
+        if (!(ok = take_w(w))) break;
+        mma_chain(tmem + 0, sA, 0, w, 0, kT / 16, id128);  // Q
+        release_w();
+        if (!(ok = take_w(w))) break;
+        mma_chain(tmem + 128, sA, 0, w, 0, kT / 16, id128);  // K
+        release_w();
+        if (!(ok = take_w(w))) break;
+        mma_chain(tmem + 256, w, 0, sA, 0, kT / 16, id128);  // V^T = Wv . h^T
+        release_w();
+        mma_commit(m2c_g);
         if (!(ok = wait_c2m())) break;  // Q, K, V^T in smem
-        mma_chain(tmem + kColS, sA, 0, sK, 0, HD / 16, id128);
-        mma_commit(m2c);
+        issue_s(0);
+        if (H > 1) issue_s(1);
         for (int h = 0; h < H && ok; ++h) {
-          if (!(ok = wait_c2m())) break;  // P_h in TMEM A
+          // P_h written over S buffer h % 2 by all compute warps.
+          if (!(ok = mbar_wait(&c2m_p[h & 1], mph_p[h & 1], p.err, kDevTimeoutOther))) break;
+          mph_p[h & 1] ^= 1;
+          tc_fence_after();
+          const uint32_t sb = (h & 1) ? kColS1 : kColS0;
+          // P_h: keys [0,64) in columns [0,32) of its S buffer, keys [64,128)
+          // in columns [64,96) (each compute warp packs over its own S half).
           for (int k = 0; k < kT / 16; ++k)
-            mma_f16_ts(tmem + kColO + h * HD, tmem + kColA + 8 * k,
+            mma_f16_ts(tmem + kColO + (h & 1) * HD, tmem + sb + (k < 4 ? 8 * k : 64 + 8 * (k - 4)),
                        op_desc(sV + static_cast<uint32_t>(h * HD * 128), 16 * k), idhd,
                        k > 0 ? 1u : 0u);
-          if (h + 1 < H)
-            mma_chain(tmem + kColS, sA, (h + 1) * HD, sK, (h + 1) * HD, HD / 16, id128);
-          mma_commit(m2c);
+          mma_commit(&m2c_o[h & 1]);
+          if (h + 2 < H) {
+            // S_{h+2} reuses the columns P_h is read from: wait until P_h.V_h
+            // has completed before overwriting them.
+            if (!(ok = mbar_wait(&m2c_o[h & 1], mph_o[h & 1], p.err, kDevTimeoutOther))) break;
+            tc_fence_after();
+            issue_s(h + 2);
+          }
+          mph_o[h & 1] ^= 1;
         }
-        if (!ok || !(ok = wait_c2m())) break;  // ctx in TMEM A
-        if (!(ok = gemm_w(0, 0))) break;
-        mma_commit(m2c);
+        if (!ok || !(ok = wait_c2m())) break;  // ctx complete in sA
+        if (!(ok = take_w(w))) break;
+        mma_chain(tmem + 0, sA, 0, w, 0, kT / 16, id128);  // out-proj
+        release_w();
+        mma_commit(m2c_g);
         if (!(ok = wait_c2m())) break;  // LN2 output in TMEM A
-        if (!(ok = gemm_w(kColF, 0))) break;
-        mma_commit(m2c);
+        if (!(ok = gemm_tmem_a(kColF))) break;
+        mma_commit(m2c_g);
         if (!(ok = wait_c2m())) break;  // GELU output in TMEM A
-        if (!(ok = gemm_w(0, 0))) break;
-        mma_commit(m2c);
+        if (!(ok = gemm_tmem_a(0))) break;
+        mma_commit(m2c_g);
       }
     }
   } else if (warp >= 2) {
     // ------------------------------------------------------------- compute
-    constexpr int HPH = HD >= 64 ? 1 : 64 / HD;  // heads covering one column half
-    const int q = warp & 3;                       // TMEM lane quarter
-    const int half = (warp - 2) >> 2;             // column / key half
-    const int bar_id = 1 + q;                     // shared with the partner warp
+    constexpr int HDH = HD / 2;  // O columns of one head handled by each warp of a pair
+    const int q = warp & 3;      // TMEM lane quarter
+    const int half = (warp - 2) >> 2;
     const int r = q * 32 + lane;
     const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16);
-    uint32_t m2c_ph = 0;
-    auto wait_m2c = [&]() {
-      // Warp-uniform outcome: a timeout seen by one lane ends the whole warp.
-      const bool ok = __all_sync(0xffffffffu, mbar_wait(m2c, m2c_ph, p.err, kDevTimeoutAccum));
-      m2c_ph ^= 1;
+    Pair pr{xch, half, r, 1 + q, 0};
+    uint32_t ph_g = 0, ph_s[2] = {0, 0}, ph_o[2] = {0, 0};
+    // Warp-uniform outcome: a timeout seen by one lane ends the whole warp.
+    auto wait = [&](uint64_t* bar, uint32_t& phase) {
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(bar, phase, p.err, kDevTimeoutAccum));
+      phase ^= 1;
       tc_fence_after();
       return ok;
     };
@@ -525,6 +500,30 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int ch_lo = (((q * 32) / S) * S) >> 5;
     const int ch_hi = (p.causal ? (q * 32 + 31) : (((q * 32 + 31) / S) * S + S - 1)) >> 5;
     const float sl2 = p.scale_log2;
+    // ctx_h = O_h / rowsum -> sA columns [h*HD + half*HD/2, +HD/2) (over Q_h).
+    auto write_ctx = [&](int h) {
+      const float l = psum[((h & 1) * 2 + 0) * kT + r] + psum[((h & 1) * 2 + 1) * kT + r];
+      const float inv = l > 0.f ? 1.0f / l : 0.f;
+      const uint32_t t_o = tl + kColO + (h & 1) * HD + half * HDH;
+      float v[HDH];
+      if constexpr (HDH == 8) {
+        uint32_t o[8];
+        tmem_ld8(t_o, o);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(o[j]) * inv;
+      } else {
+#pragma unroll
+        for (int c = 0; c < HDH / 16; ++c) {
+          uint32_t o[16];
+          tmem_ld16(t_o + 16 * c, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[16 * c + j] = __uint_as_float(o[j]) * inv;
+        }
+      }
+      store_row<HDH / 8>(sA, r, h * HD + half * HDH, v);
+    };
     bool ok = true;
     for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
       const int64_t grow = static_cast<int64_t>(tile) * kT + r;
@@ -535,7 +534,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       // A chunk needs no masking when every key in it is valid for every row
       // of this warp: whole-tile sequences, no padding, below the diagonal.
       const bool plain_tile = (S == kT) && (p.valid_len == nullptr);
-      int slot = 0;
       float xv[2][32];  // this warp's 64 columns of the fp32 residual row
       {
         const float4* x4 = reinterpret_cast<const float4*>(p.x + grow * kT + 64 * half);
@@ -556,41 +554,54 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tmem_st_wait();
       }
-      pair_ln_to_smem(xv, tl, slot, half, bar_id, p.eps, par + kPLn1g, par + kPLn1b, sA, r);
+      {
+        float mean, rstd, v[2][32];
+        row_stats(xv, pr, p.eps, mean, rstd);
+        ln_apply(xv, mean, rstd, par + kPLn1g, par + kPLn1b, half, v);
+        store_row<4>(sA, r, 64 * half, v[0]);
+        store_row<4>(sA, r, 64 * half + 32, v[1]);
+      }
       for (int l = 0; l < L; ++l) {
         const float* lp = par + l * kParFloats;
         signal();  // LN1 output in sA
-        if (!(ok = wait_m2c())) break;
-        // QKV epilogue: this half takes Q (or K) plus half of V.
+        if (!(ok = wait(m2c_g, ph_g))) break;
+        // QKV epilogue: half 0 takes Q and the first half of the tokens of
+        // V^T row r; half 1 takes K and the second half. V^T lanes are features.
+        {
+          const float bv = lp[kPQkv + 256 + r];  // V bias of feature r
 #pragma unroll 1
-        for (int i = 0; i < 6; ++i) {
-          const int c = i < 4 ? 4 * half + i : 8 + 2 * half + (i - 4);
-          float v[32];
-          tmem_ld_row(tl + 32 * c, v);
-          add_bias32(v, lp + kPQkv + 32 * c);
-          if (c < 4)
-            store_row32(sA, r, 32 * c, v);
-          else if (c < 8)
-            store_row32(sK, r, 32 * (c - 4), v);
-          else
-            store_vt32(sV, r, 32 * (c - 8), v);
+          for (int i = 0; i < 6; ++i) {
+            float v[32];
+            if (i < 4) {
+              const int c = 4 * half + i;  // Q chunks 0..3 or K chunks 4..7
+              tmem_ld_row(tl + 32 * c, v);
+              add_bias32(v, lp + kPQkv + 32 * c);
+              store_row<4>(half == 0 ? sA : sK, r, 32 * i, v);
+            } else {
+              const int c = 2 * half + (i - 4);  // token chunk of V^T row r
+              tmem_ld_row(tl + 256 + 32 * c, v);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] += bv;
+              store_row<4>(sV, r, 32 * c, v);
+            }
+          }
         }
-        slot = 2;  // exchange slots 0, 1 were the LN1 statistics
         signal();
-        // Attention, one head at a time; this warp owns keys [64*half, +64).
+        // Attention, double-buffered over heads.
 #pragma unroll 1
         for (int h = 0; h < H; ++h) {
-          if (!(ok = wait_m2c())) break;
+          const int b = h & 1;
+          const uint32_t sb = tl + (b ? kColS1 : kColS0);
+          if (!(ok = wait(&m2c_s[b], ph_s[b]))) break;
           // Two passes over this warp's (at most two) 32-key chunks so only
-          // one chunk is live in registers: masked row max, then exp2 + sum
-          // + fp16 packing into the TMEM A operand.
+          // one chunk is live: masked row max, then exp2 + sum + fp16 packing.
           float mx = -INFINITY;
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             const int ch = 2 * half + c;
             if (ch >= ch_lo && ch <= ch_hi) {  // warp-uniform
               float sc[32];
-              tmem_ld_row(tl + kColS + 32 * ch, sc);
+              tmem_ld_row(sb + 32 * ch, sc);
               if (plain_tile && (!p.causal || ch < q)) {
 #pragma unroll
                 for (int j = 0; j < 32; ++j) mx = fmaxf(mx, sc[j]);
@@ -603,7 +614,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
           }
-          mx = pair_combine<true>(tl, slot++, half, bar_id, mx);
+          mx = fmaxf(mx, pr.swap(make_float2(mx, 0.f)).x);
           // All keys padding (zero-length sequence): weights exp2(-inf) = 0.
           const float mref = (mx == -INFINITY) ? 0.f : mx * sl2;
           float sum = 0.f;
@@ -613,7 +624,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int ch = 2 * half + c;
             if (ch >= ch_lo && ch <= ch_hi) {
               float sc[32];
-              tmem_ld_row(tl + kColS + 32 * ch, sc);
+              tmem_ld_row(sb + 32 * ch, sc);
               const bool plain = plain_tile && (!p.causal || ch < q);
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
@@ -630,61 +641,68 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int j = 0; j < 16; ++j) w[16 * c + j] = 0u;
             }
           }
-          tmem_st1(tl + kColSum + 2 * h + half, __float_as_uint(sum));
-          tmem_st32(tl + kColA + 32 * half, w);
+          psum[(b * 2 + half) * kT + r] = sum;
+          tmem_st32(sb + 64 * half, w);  // P over this warp's own S columns
           tmem_st_wait();
-          signal();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&c2m_p[b]);
+          if (h > 0) {  // overlap: finish the previous head while P.V runs
+            if (!(ok = wait(&m2c_o[b ^ 1], ph_o[b ^ 1]))) break;
+            write_ctx(h - 1);
+          }
         }
-        if (!ok || !(ok = wait_m2c())) break;  // last P.V done
+        if (!ok || !(ok = wait(&m2c_o[(H - 1) & 1], ph_o[(H - 1) & 1]))) break;
+        named_bar_sync(pr.bar_id, 64);  // partner's row sum of the last head is visible
+        write_ctx(H - 1);
+        signal();  // ctx complete
+        if (!(ok = wait(m2c_g, ph_g))) break;  // out-proj accumulator
         {
-          // ctx = O / rowsum for this half's columns.
-          const int h0 = (64 * half) / HD;
-          uint32_t sums[16];
-          tmem_ld16(tl + kColSum + 2 * h0, sums);
-          tmem_ld_wait();
-          float inv[HPH];
-#pragma unroll
-          for (int k = 0; k < HPH; ++k) {
-            const float lsum = __uint_as_float(sums[2 * k]) + __uint_as_float(sums[2 * k + 1]);
-            inv[k] = lsum > 0.f ? 1.0f / lsum : 0.f;
-          }
-          float v[2][32];
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            tmem_ld_row(tl + kColO + 64 * half + 32 * c, v[c]);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[c][j] *= inv[HD >= 64 ? 0 : (32 * c + j) / HD];
-          }
+          float mean, rstd, v[2][32];
+          residual_add(tl, tl, half, lp + kPOut, xv);
+          row_stats(xv, pr, p.eps, mean, rstd);
+          ln_apply(xv, mean, rstd, lp + kPLn2g, lp + kPLn2b, half, v);
           store_a_tmem(tl, half, v);
         }
         signal();
-        if (!(ok = wait_m2c())) break;  // out-proj accumulator
-        pair_residual_add(tl, tl, half, lp + kPOut, xv);
-        pair_ln_to_tmem(xv, tl, slot, half, bar_id, p.eps, lp + kPLn2g, lp + kPLn2b);
-        signal();
-        if (!(ok = wait_m2c())) break;  // FFN-in accumulator
+        if (!(ok = wait(m2c_g, ph_g))) break;  // FFN-in accumulator
         {
           float v[2][32];
-#pragma unroll 1
+#pragma unroll
           for (int c = 0; c < 2; ++c) {
             const int col = 64 * half + 32 * c;
             tmem_ld_row(tl + kColF + col, v[c]);
             add_bias32(v[c], lp + kPIn + col);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[c][j] = gelu_erf(v[c][j]);
+            for (int j = 0; j < 32; ++j) v[c][j] = gelu_as(v[c][j]);
           }
           store_a_tmem(tl, half, v);
         }
         signal();
-        if (!(ok = wait_m2c())) break;  // FFN-out accumulator
-        pair_residual_add(tl, tl, half, lp + kPFo, xv);
-        slot = 0;
-        if (l + 1 < L) {
-          pair_ln_to_smem(xv, tl, slot, half, bar_id, p.eps, lp + kParFloats + kPLn1g,
-                          lp + kParFloats + kPLn1b, sA, r);
-        } else {
-          pair_ln_to_global(xv, tl, slot, half, bar_id, p.eps, parf, parf + 128,
-                            p.y + grow * kT, row_ok ? (row_valid ? 1 : 2) : 0);
+        if (!(ok = wait(m2c_g, ph_g))) break;  // FFN-out accumulator
+        {
+          float mean, rstd, v[2][32];
+          residual_add(tl, tl, half, lp + kPFo, xv);
+          row_stats(xv, pr, p.eps, mean, rstd);
+          if (l + 1 < L) {
+            ln_apply(xv, mean, rstd, lp + kParFloats + kPLn1g, lp + kParFloats + kPLn1b, half,
+                     v);
+            store_row<4>(sA, r, 64 * half, v[0]);
+            store_row<4>(sA, r, 64 * half + 32, v[1]);
+          } else {
+            ln_apply(xv, mean, rstd, parf, parf + 128, half, v);
+            if (row_ok) {  // final output: padded tokens are zero rows
+              const float keep = row_valid ? 1.0f : 0.0f;
+              float4* y4 = reinterpret_cast<float4*>(p.y + grow * kT + 64 * half);
+#pragma unroll
+              for (int c = 0; c < 2; ++c)
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                  __stcs(y4 + 8 * c + j,
+                         make_float4(v[c][4 * j] * keep, v[c][4 * j + 1] * keep,
+                                     v[c][4 * j + 2] * keep, v[c][4 * j + 3] * keep));
+            }
+          }
         }
       }
     }

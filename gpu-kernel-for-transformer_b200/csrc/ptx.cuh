@@ -223,6 +223,14 @@ __device__ __forceinline__ void tmem_st1(uint32_t taddr, uint32_t r) {
   asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr), "r"(r) : "memory");
 }
 
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                 "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr)
+               : "memory");
+}
+
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -296,6 +304,33 @@ __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// 1/x with the hardware approximation (rcp.approx.ftz.f32).
+__device__ __forceinline__ float fast_rcp(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// GELU in its exact form x * Phi(x), Phi(x) = (1 + erf(x / sqrt 2)) / 2, with
+// erf from Abramowitz & Stegun, Handbook of Mathematical Functions, 7.1.26:
+//   erf(z) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-z^2),
+//   t = 1 / (1 + p z), z >= 0, |error| <= 1.5e-7,
+// p = 0.3275911, a1..a5 = 0.254829592, -0.284496736, 1.421413741,
+// -1.453152027, 1.061405429. For x < 0 the tail term is used directly
+// (Phi(x) = (1 - erf(|z|)) / 2), so there is no cancellation. Branch-free;
+// |Phi error| <= 7.5e-8, far below the fp16 rounding of the result.
+__device__ __forceinline__ float gelu_as(float x) {
+  const float z = fabsf(x) * 0.70710678118654752f;
+  const float t = fast_rcp(fmaf(0.3275911f, z, 1.0f));
+  float poly = fmaf(1.061405429f, t, -1.453152027f);
+  poly = fmaf(poly, t, 1.421413741f);
+  poly = fmaf(poly, t, -0.284496736f);
+  poly = fmaf(poly, t, 0.254829592f);
+  poly *= t;
+  const float half_tail = 0.5f * poly * fast_exp2(-1.4426950408889634f * z * z);
+  return x * (x >= 0.f ? 1.0f - half_tail : half_tail);
 }
 
 // Named barrier over `count` threads (a multiple of 32) with id `id` (1..15).

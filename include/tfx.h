@@ -148,7 +148,7 @@ typedef struct tfx_model {
 /*
  * Path policy of tfx_forward for this process: 1 (default) runs the fused
  * whole-forward kernel wherever it applies (d_model = ffn_dim = 128, seq_len
- * dividing 128, head_dim in {16, 32, 64, 128}, <= 8 layers; with or without
+ * dividing 128, head_dim in {16, 32, 64, 128}, <= 5 layers; with or without
  * valid_len); 0 always runs the per-op kernel chain. Returns the previous
  * policy. Query tfx_forward_workspace_bytes again after changing it.
  * No reference counterpart (the reference's toggles are per-module:
