@@ -39,6 +39,12 @@
 //   m: acc = h2 . W1^T         c: g = gelu(acc + b1) -> TMEM A operand
 //   m: acc = g . W2^T          c: x += acc + b2; next LN1 or final LN -> y
 //
+// Causal balance: TMEM lane quarter q is served by SM sub-partition q, and
+// under a causal mask the last quarter of query rows has four times the work
+// of the first. Odd heads therefore place query row t of the tile in S/P/O
+// row 127-t (the QKV epilogue writes Q_h rows reversed; ctx_h is written back
+// in token order), so every sub-partition gets the same total over two heads.
+//
 // tcgen05.ld/st are warp-collective: every TMEM access of the compute warps
 // is executed by all 32 lanes; rows past the end of the batch and padded
 // tokens are handled by predicating only the global stores.
@@ -125,6 +131,21 @@ __device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, ui
                : "memory");
 }
 
+// Query rows of odd heads are stored reversed (row 127 - t): see the
+// causal-balance note at the top of the file. Columns [c0, c0+32) of token
+// row t's Q, head of each 8-column group = column / HD.
+template <int HD>
+__device__ __forceinline__ void store_q32(uint32_t base, int t, int c0, const float* v) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int col = c0 + 8 * j;
+    const int row = ((col / HD) & 1) ? (kT - 1 - t) : t;
+    sts128(sw_addr(base, row, col), pack_half2(v[8 * j], v[8 * j + 1]),
+           pack_half2(v[8 * j + 2], v[8 * j + 3]), pack_half2(v[8 * j + 4], v[8 * j + 5]),
+           pack_half2(v[8 * j + 6], v[8 * j + 7]));
+  }
+}
+
 // Row r, columns [c0, c0 + 8*N8) of a K-major operand <- fp16(v).
 template <int N8>
 __device__ __forceinline__ void store_row(uint32_t base, int r, int c0, const float* v) {
@@ -192,20 +213,21 @@ struct Pair {
 // same numbers in the same order.
 __device__ __forceinline__ void row_stats(const float (&x)[2][32], Pair& pr, float eps,
                                           float& mean, float& rstd) {
-  float s = 0.f;
+  float s4[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums: short dependency chains
 #pragma unroll
   for (int c = 0; c < 2; ++c)
 #pragma unroll
-    for (int j = 0; j < 32; ++j) s += x[c][j];
-  const float m_half = s * (1.0f / 64.0f);
-  float q = 0.f;
+    for (int j = 0; j < 32; ++j) s4[j & 3] += x[c][j];
+  const float m_half = ((s4[0] + s4[1]) + (s4[2] + s4[3])) * (1.0f / 64.0f);
+  float q4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int c = 0; c < 2; ++c)
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       const float t = x[c][j] - m_half;
-      q = fmaf(t, t, q);
+      q4[j & 3] = fmaf(t, t, q4[j & 3]);
     }
+  const float q = (q4[0] + q4[1]) + (q4[2] + q4[3]);
   const float2 o = pr.swap(make_float2(m_half, q));
   const float m0 = pr.half == 0 ? m_half : o.x, m1 = pr.half == 0 ? o.x : m_half;
   const float q0 = pr.half == 0 ? q : o.y, q1 = pr.half == 0 ? o.y : q;
@@ -493,12 +515,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(c2m);
     };
     const int S = p.seq;
-    // Key range of this thread's row (own sequence; causal) and the
+    // Per head parity (odd heads: reversed rows): the query token of this
+    // lane's S row, its key range (own sequence; causal) and the
     // warp-uniform range of 32-key chunks that can hold a valid key.
-    const int seq_lo = (r / S) * S;
-    const int key_hi_nopad = p.causal ? r : seq_lo + S - 1;
-    const int ch_lo = (((q * 32) / S) * S) >> 5;
-    const int ch_hi = (p.causal ? (q * 32 + 31) : (((q * 32 + 31) / S) * S + S - 1)) >> 5;
+    // (Scalars selected by parity, not arrays: a runtime index would put
+    // them in local memory.)
+    const int tok0 = r, tok1 = kT - 1 - r;
+    const int qq0 = q, qq1 = 3 - q;  // quarter of the tokens this warp holds
+    const int seq_lo0 = (tok0 / S) * S, seq_lo1 = (tok1 / S) * S;
+    const int khn0 = p.causal ? tok0 : seq_lo0 + S - 1;
+    const int khn1 = p.causal ? tok1 : seq_lo1 + S - 1;
+    auto chunk_lo = [&](int qx) { return (((qx * 32) / S) * S) >> 5; };
+    auto chunk_hi = [&](int qx) {
+      return (p.causal ? (qx * 32 + 31) : (((qx * 32 + 31) / S) * S + S - 1)) >> 5;
+    };
+    const int ch_lo0 = chunk_lo(qq0), ch_lo1 = chunk_lo(qq1);
+    const int ch_hi0 = chunk_hi(qq0), ch_hi1 = chunk_hi(qq1);
     const float sl2 = p.scale_log2;
     // ctx_h = O_h / rowsum -> sA columns [h*HD + half*HD/2, +HD/2) (over Q_h).
     auto write_ctx = [&](int h) {
@@ -522,15 +554,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < 16; ++j) v[16 * c + j] = __uint_as_float(o[j]) * inv;
         }
       }
-      store_row<HDH / 8>(sA, r, h * HD + half * HDH, v);
+      store_row<HDH / 8>(sA, (h & 1) ? tok1 : tok0, h * HD + half * HDH, v);  // token order
     };
     bool ok = true;
     for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
       const int64_t grow = static_cast<int64_t>(tile) * kT + r;
       const bool row_ok = grow < p.rows;
+      const int64_t gt1 = static_cast<int64_t>(tile) * kT + tok1;
       const int len = (p.valid_len != nullptr && row_ok) ? p.valid_len[grow / S] : S;
-      const int key_hi = min(key_hi_nopad, seq_lo + len - 1);  // padded keys masked
-      const bool row_valid = (r - seq_lo) < len;                // not a padded token
+      const int len1 = (p.valid_len != nullptr && gt1 < p.rows) ? p.valid_len[gt1 / S] : S;
+      const int key_hi0 = min(khn0, seq_lo0 + len - 1);  // padded keys masked
+      const int key_hi1 = min(khn1, seq_lo1 + len1 - 1);
+      const bool row_valid = (r - seq_lo0) < len;  // not a padded token
       // A chunk needs no masking when every key in it is valid for every row
       // of this warp: whole-tile sequences, no padding, below the diagonal.
       const bool plain_tile = (S == kT) && (p.valid_len == nullptr);
@@ -570,19 +605,34 @@ __global__ void __launch_bounds__(kThreads, 1)
         {
           const float bv = lp[kPQkv + 256 + r];  // V bias of feature r
 #pragma unroll 1
-          for (int i = 0; i < 6; ++i) {
-            float v[32];
-            if (i < 4) {
-              const int c = 4 * half + i;  // Q chunks 0..3 or K chunks 4..7
-              tmem_ld_row(tl + 32 * c, v);
-              add_bias32(v, lp + kPQkv + 32 * c);
-              store_row<4>(half == 0 ? sA : sK, r, 32 * i, v);
-            } else {
-              const int c = 2 * half + (i - 4);  // token chunk of V^T row r
-              tmem_ld_row(tl + 256 + 32 * c, v);
+          for (int i = 0; i < 6; i += 2) {  // two chunks per TMEM wait
+            // i < 4: Q chunks 0..3 (half 0) or K chunks 4..7 (half 1);
+            // i >= 4: token chunks of V^T row r.
+            const uint32_t col0 = i < 4 ? 32 * (4 * half + i) : 256 + 32 * (2 * half + i - 4);
+            uint32_t ra[32], rb[32];
+            tmem_ld32(tl + col0, ra);
+            tmem_ld32(tl + col0 + 32, rb);
+            tmem_ld_wait();
+            float v[2][32];
 #pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] += bv;
-              store_row<4>(sV, r, 32 * c, v);
+            for (int j = 0; j < 32; ++j) {
+              v[0][j] = __uint_as_float(ra[j]);
+              v[1][j] = __uint_as_float(rb[j]);
+            }
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              if (i < 4) {
+                const int c = 4 * half + i + u;
+                add_bias32(v[u], lp + kPQkv + 32 * c);
+                if (half == 0)
+                  store_q32<HD>(sA, r, 32 * (i + u), v[u]);
+                else
+                  store_row<4>(sK, r, 32 * (i + u), v[u]);
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[u][j] += bv;
+                store_row<4>(sV, r, 32 * (2 * half + i - 4 + u), v[u]);
+              }
             }
           }
         }
@@ -593,46 +643,54 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int b = h & 1;
           const uint32_t sb = tl + (b ? kColS1 : kColS0);
           if (!(ok = wait(&m2c_s[b], ph_s[b]))) break;
-          // Two passes over this warp's (at most two) 32-key chunks so only
-          // one chunk is live: masked row max, then exp2 + sum + fp16 packing.
-          float mx = -INFINITY;
+          // Odd heads use the reversed-row key ranges.
+          const int lo_e = b ? ch_lo1 : ch_lo0, hi_e = b ? ch_hi1 : ch_hi0;
+          const int qq_e = b ? qq1 : qq0;
+          const int kl_e = b ? seq_lo1 : seq_lo0, kh_e = b ? key_hi1 : key_hi0;
+          bool in[2], plain[2];
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             const int ch = 2 * half + c;
-            if (ch >= ch_lo && ch <= ch_hi) {  // warp-uniform
-              float sc[32];
-              tmem_ld_row(sb + 32 * ch, sc);
-              if (plain_tile && (!p.causal || ch < q)) {
+            in[c] = ch >= lo_e && ch <= hi_e;  // warp-uniform
+            plain[c] = plain_tile && (!p.causal || ch < qq_e);
+          }
+          // Pass 1: masked row max (one chunk live at a time).
+          float mx = -INFINITY;
 #pragma unroll
-                for (int j = 0; j < 32; ++j) mx = fmaxf(mx, sc[j]);
-              } else {
+          for (int c = 0; c < 2; ++c) {
+            if (!in[c]) continue;
+            float sc[32];
+            tmem_ld_row(sb + 64 * half + 32 * c, sc);
+            const int k0 = 32 * (2 * half + c);
+            if (plain[c]) {
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                  const int key = 32 * ch + j;
-                  if (key >= seq_lo && key <= key_hi) mx = fmaxf(mx, sc[j]);
-                }
+              for (int j = 0; j < 32; ++j) mx = fmaxf(mx, sc[j]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const int key = k0 + j;
+                if (key >= kl_e && key <= kh_e) mx = fmaxf(mx, sc[j]);
               }
             }
           }
           mx = fmaxf(mx, pr.swap(make_float2(mx, 0.f)).x);
           // All keys padding (zero-length sequence): weights exp2(-inf) = 0.
           const float mref = (mx == -INFINITY) ? 0.f : mx * sl2;
-          float sum = 0.f;
+          // Pass 2: exp2, row sum, fp16 packing.
+          float sum2[2] = {0.f, 0.f};
           uint32_t w[32];
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
-            const int ch = 2 * half + c;
-            if (ch >= ch_lo && ch <= ch_hi) {
+            if (in[c]) {
               float sc[32];
-              tmem_ld_row(sb + 32 * ch, sc);
-              const bool plain = plain_tile && (!p.causal || ch < q);
+              tmem_ld_row(sb + 64 * half + 32 * c, sc);
+              const int k0 = 32 * (2 * half + c);
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
-                const int key = 32 * ch + j;
-                float e = fast_exp2(fmaf(sc[j], sl2, -mref));
-                if (!plain && (key < seq_lo || key > key_hi)) e = 0.f;
-                sc[j] = e;
-                sum += e;
+                float ex = fast_exp2(fmaf(sc[j], sl2, -mref));
+                if (!plain[c] && (k0 + j < kl_e || k0 + j > kh_e)) ex = 0.f;
+                sc[j] = ex;
+                sum2[j & 1] += ex;
               }
 #pragma unroll
               for (int j = 0; j < 16; ++j) w[16 * c + j] = pack_half2(sc[2 * j], sc[2 * j + 1]);
@@ -641,6 +699,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int j = 0; j < 16; ++j) w[16 * c + j] = 0u;
             }
           }
+          const float sum = sum2[0] + sum2[1];
           psum[(b * 2 + half) * kT + r] = sum;
           tmem_st32(sb + 64 * half, w);  // P over this warp's own S columns
           tmem_st_wait();
