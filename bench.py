@@ -480,11 +480,10 @@ def main():
             fg.replay()
             barrier()
             t0 = time.perf_counter()
-            bufs = [torch.empty_like(y) for _ in range(world)] if rank == 0 else None
-            dist.gather(y, bufs, dst=0)
+            full = pkg.sharding.gather_shards(y, world * B, dst=0)
             torch.cuda.synchronize()
             gather_ms = (time.perf_counter() - t0) * 1e3
-            del bufs
+            del full
 
     fwd_flops = flops_per_token(S, D, H, F, L) * tokens_per_step
     cpu = None

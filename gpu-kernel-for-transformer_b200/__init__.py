@@ -10,7 +10,7 @@ The directory name is not a Python identifier; import it with
 ``importlib.import_module("gpu-kernel-for-transformer_b200")``.
 """
 
-from . import _lib, ops  # noqa: F401
+from . import _lib, ops, sharding  # noqa: F401
 from .graph import FixedInputCUDAGraph, ForwardGraph, maybe_cuda_graph  # noqa: F401
 from .model import (  # noqa: F401
     OFFICIAL_BENCHMARK_SHAPES,
@@ -30,6 +30,7 @@ __all__ = [
     "ForwardGraph",
     "maybe_cuda_graph",
     "ops",
+    "sharding",
 ]
 
 
