@@ -291,6 +291,10 @@ int launch_hd(const __half* q, const __half* k, const __half* v, int64_t ld_qkv,
 int launch_attention(const __half* q, const __half* k, const __half* v, int64_t ld_qkv,
                      __half* out, int64_t ld_out, int batch, int heads, int seq, int head_dim,
                      float scale, int causal, const int32_t* valid_len, cudaStream_t stream) {
+  // Head dims 64 and 128 run on the tcgen05 kernel (attention_tc.cu).
+  if (attention_tc_supported(head_dim, scale))
+    return launch_attention_tc(q, k, v, ld_qkv, out, ld_out, batch, heads, seq, head_dim, scale,
+                               causal, valid_len, stream);
   switch (head_dim) {
     case 8:
       return launch_hd<8>(q, k, v, ld_qkv, out, ld_out, batch, heads, seq, scale, causal,

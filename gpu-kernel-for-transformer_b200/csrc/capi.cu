@@ -82,9 +82,8 @@ int ensure_smem(const void* func, int bytes, int* done_flags) {
   return TFX_OK;
 }
 
-int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes,
-                 uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_cols, uint32_t box_rows,
-                 CUtensorMapSwizzle swizzle) {
+// cuTensorMapEncodeTiled, looked up once through the runtime.
+static int resolve_encode() {
   if (g_encode == nullptr) {
     std::lock_guard<std::mutex> lock(g_mu);
     if (g_encode == nullptr) {
@@ -97,6 +96,13 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
       g_encode = reinterpret_cast<EncodeTiledFn>(fn);
     }
   }
+  return TFX_OK;
+}
+
+int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes,
+                 uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_cols, uint32_t box_rows,
+                 CUtensorMapSwizzle swizzle) {
+  if (int st = resolve_encode()) return st;
   const cuuint64_t dims[2] = {cols, rows};
   const cuuint64_t strides[1] = {ld * static_cast<uint64_t>(elem_bytes)};
   const cuuint32_t box[2] = {box_cols, box_rows};
@@ -109,6 +115,23 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
     return fail(TFX_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d): rows=%llu cols=%llu ld=%llu",
                 static_cast<int>(r), (unsigned long long)rows, (unsigned long long)cols,
                 (unsigned long long)ld);
+  return TFX_OK;
+}
+
+int make_tmap_3d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t batch, uint64_t cols,
+                 uint64_t ld, uint64_t batch_stride, uint32_t box_cols, uint32_t box_rows) {
+  if (int st = resolve_encode()) return st;
+  const cuuint64_t dims[3] = {cols, rows, batch};
+  const cuuint64_t strides[2] = {ld * 2, batch_stride * 2};
+  const cuuint32_t box[3] = {box_cols, box_rows, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base),
+                              dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(TFX_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed (%d): rows=%llu batch=%llu",
+                static_cast<int>(r), (unsigned long long)rows, (unsigned long long)batch);
   return TFX_OK;
 }
 

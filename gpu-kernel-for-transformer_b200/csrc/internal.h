@@ -37,6 +37,12 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
                  uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_cols, uint32_t box_rows,
                  CUtensorMapSwizzle swizzle);
 
+// 3-D fp16 view [batch][rows][cols] (row pitch `ld`, batch pitch
+// `batch_stride`, both in elements) with a box of box_cols x box_rows x 1 and
+// the 128-byte swizzle. Rows past `rows` inside a batch read as zeros.
+int make_tmap_3d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t batch, uint64_t cols,
+                 uint64_t ld, uint64_t batch_stride, uint32_t box_cols, uint32_t box_rows);
+
 // Kernel launchers (validated by the C-ABI layer before they are called).
 int launch_layer_norm(const float* x, const float* gamma, const float* beta, void* y, int y_dtype,
                       int64_t rows, int d, float eps, int apply_affine, cudaStream_t stream);
@@ -50,6 +56,12 @@ int launch_linear(const __half* a, int64_t lda, const __half* w, const float* bi
 int launch_attention(const __half* q, const __half* k, const __half* v, int64_t ld_qkv,
                      __half* out, int64_t ld_out, int batch, int heads, int seq, int head_dim,
                      float scale, int causal, const int32_t* valid_len, cudaStream_t stream);
+
+// tcgen05/TMEM flash attention for head_dim 64 and 128 (scale > 0).
+bool attention_tc_supported(int head_dim, float scale);
+int launch_attention_tc(const __half* q, const __half* k, const __half* v, int64_t ld_qkv,
+                        __half* out, int64_t ld_out, int batch, int heads, int seq, int head_dim,
+                        float scale, int causal, const int32_t* valid_len, cudaStream_t stream);
 
 // Whole-forward fused kernel (d_model = ffn_dim = 128, seq | 128).
 bool fused_forward_supported(const tfx_model* m, int seq, const int32_t* valid_len);

@@ -95,6 +95,15 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
+                                            int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* smem_src, int c0,
                                              int c1) {
   asm volatile(
@@ -282,6 +291,23 @@ __device__ __forceinline__ uint64_t sdesc_k_sw128(uint32_t smem_addr) {
   return d;
 }
 
+// Shared-memory descriptor for an MN-major operand with the 128-byte swizzle:
+// the tile is stored as rows along K (one 128-byte row = 64 fp16 along M/N),
+// 8-row atoms of 1024 B stacked along K (stride byte offset 1024), and
+// further 64-wide blocks along M/N `lbo_bytes` apart (leading byte offset).
+// This is exactly a row-major [K rows x 64 cols] tile written by TMA with
+// CU_TENSOR_MAP_SWIZZLE_128B, e.g. a V tile [keys x head_dim] used as the B
+// operand of P.V. Advancing K by 16 adds 16 rows = 2048 bytes.
+__device__ __forceinline__ uint64_t sdesc_mn_sw128(uint32_t smem_addr, uint32_t lbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFF);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFF) << 16;
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(2) << 61;
+  return d;
+}
+
 // Instruction descriptor, kind::f16: fp16 A and B (both K-major), fp32 D,
 // shape M x N (M in {64,128}, N a multiple of 16 up to 256).
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n) {
@@ -290,6 +316,11 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n) {
          | (0u << 15) | (0u << 16)                  // A, B K-major
          | (static_cast<uint32_t>(n >> 3) << 17)    // N >> 3
          | (static_cast<uint32_t>(m >> 4) << 24);   // M >> 4
+}
+
+// Same, with the B operand MN-major (bit 16).
+__host__ __device__ constexpr uint32_t idesc_f16_f32_bmn(int m, int n) {
+  return idesc_f16_f32(m, n) | (1u << 16);
 }
 
 // ------------------------------------------------------------ conversions

@@ -128,6 +128,12 @@ ATTN_CASES = [
     (2, 70, 8, 16, True),
     (2, 100, 4, 32, False),
     (1, 64, 2, 256, False),
+    # head_dim 64/128 run on the tcgen05 kernel: two query tiles per CTA, a
+    # ragged last query block, several KV tiles, non-causal.
+    (2, 384, 2, 64, True),
+    (2, 257, 4, 64, False),
+    (1, 513, 2, 128, False),
+    (3, 129, 2, 128, True),
 ]
 
 
@@ -142,10 +148,12 @@ def test_attention(pkg, dev, b, s, h, hd, causal):
     assert err < 2e-3, err
 
 
-def test_attention_key_padding(pkg, dev):
-    b, s, h, hd = 3, 128, 4, 32
-    qkv = _randn(b, s, 3, h, hd, seed=11).half()
-    lengths = torch.tensor([128, 97, 5], dtype=torch.int32)
+@pytest.mark.parametrize("s,hd", [(128, 32), (300, 64), (300, 128)])
+def test_attention_key_padding(pkg, dev, s, hd):
+    """Keys at or past valid_len are masked; length 0 gives a zero output."""
+    b, h = 4, 4
+    qkv = _randn(b, s, 3, h, hd, seed=11 + hd).half()
+    lengths = torch.tensor([s, 97, 5, 0], dtype=torch.int32)
     ref = _attn_ref(qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2], True, lengths)
     g = qkv.to(dev)
     got = pkg.ops.attention(g[:, :, 0], g[:, :, 1], g[:, :, 2], is_causal=True,
