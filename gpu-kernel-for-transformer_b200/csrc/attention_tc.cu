@@ -1,22 +1,36 @@
 // Flash attention on the 5th-generation tensor cores, head_dim 64 and 128.
 //
 // CTA = 256 query rows of one (batch, head), split into two 128-row tiles A
-// and B that share every K/V tile; 10 warps, one CTA per SM:
+// and B that share every K/V tile; 11 warps, one CTA per SM:
 //   warp 0      TMA producer (one lane): Q_A and Q_B once, then K_j and V_j
 //               into a ring of shared-memory stages
-//   warp 1      TMEM owner (all 512 columns) + MMA issuer (one lane)
+//   warp 1      TMEM owner (all 512 columns) + MMA issuer of tile A (one lane)
+//   warp 10     MMA issuer of tile B (one lane)
 //   warps 2..5  softmax of tile A, warps 6..9 softmax of tile B; thread =
 //               query row = TMEM lane, so no cross-thread reductions
-// TMEM columns: S_A [0,128), S_B [128,256), O_A [256,256+HD), O_B after it.
+// tcgen05.mma issue blocks while the tensor core's short instruction queue
+// is full; with one issuer per tile, one tile's commits and barrier waits
+// overlap the other tile's queued products instead of draining the queue.
+// TMEM columns (512):
+//   HD 64:  S_A [0,128) S_B [128,256) P_A [256,320) P_B [320,384) O_A, O_B
+//   HD 128: S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512), and P_X
+//           is written over the first 64 columns of S_X
 //
 // Per KV tile j and query tile X:
 //   S_X  = Q_X K_j^T      SS MMA 128x128xHD, fp32 into TMEM
 //   softmax warps         row max; lazy rescale of O_X; P = 2^(S*c - m) as
-//                         fp16, written over the first 64 columns of S_X
-//   O_X += P V_j          TS MMA: P straight from TMEM, V_j read MN-major
-//                         from its row-major [keys x HD] tile
-// The tensor core works on one tile's products while the other tile's
-// softmax runs (A and B ping-pong), so neither unit waits for the other.
+//                         fp16 into TMEM
+//   O_X += P V_j          TS MMA, P straight from TMEM. V_j comes either
+//                         K-major from a transposed copy V^T [b][h][d][s]
+//                         (the forward path; full-rate MMAs) or MN-major
+//                         from the row-major [keys x HD] tile (the plain
+//                         tfx_attention call, whose MMAs run about half as
+//                         fast with an MN-major operand)
+// With a separate P region (HD 64) S_X(j+1) is computed as soon as the
+// softmax warps hold S_X(j) in registers, so the softmax of consecutive KV
+// tiles runs back to back and only the P store waits for PV_X(j-1). The two
+// query tiles' softmax warps share each SM sub-partition, so one tile's
+// loads and reductions hide behind the other tile's exponentials.
 //
 // Lazy rescaling: a row's reference max m only moves when its running max
 // exceeds m by more than 8 (log2 units). P is then at most 2^8, fine in fp16,
@@ -38,7 +52,7 @@
 namespace tfx {
 namespace {
 
-constexpr int kTcThreads = 320;
+constexpr int kTcThreads = 352;
 constexpr int kTile = 128;            // query rows per tile = keys per KV tile
 constexpr float kRescaleLog2 = 8.0f;  // lazy-rescale threshold (P <= 2^8)
 constexpr uint32_t kTmemCols = 512;
@@ -49,17 +63,21 @@ struct TcAttn {
   static constexpr int kBlocks = HD / 64;            // 128-byte column blocks per row
   static constexpr int kBlockBytes = kTile * 128;    // one 64-column block of a tile
   static constexpr int kTileBytes = kTile * HD * 2;  // one Q/K/V tile, fp16
+  static constexpr int kVtBoxBytes = HD * 128;        // V^T box: HD rows x 64 keys
   static constexpr int kQ = 0;                        // Q_A, Q_B
   static constexpr int kK = 2 * kTileBytes;
   static constexpr int kV = kK + kStages * kTileBytes;
   static constexpr int kBar = kV + kStages * kTileBytes;
   static constexpr int kSmem = kBar + 256 + 1024;    // barriers + alignment slack
-  static constexpr uint32_t kColO = 2 * kTile;
+  static constexpr bool kSepP = HD == 64;                 // P has its own TMEM columns
+  static constexpr uint32_t kColP = kSepP ? 2 * kTile : 0;
+  static constexpr uint32_t kPStride = kSepP ? kTile / 2 : kTile;
+  static constexpr uint32_t kColO = kSepP ? 3 * kTile : 2 * kTile;
   static_assert(kColO + 2 * HD <= kTmemCols, "TMEM budget");
   static_assert(kSmem <= 227 * 1024, "shared-memory budget");
 };
 
-template <int HD, bool CAUSAL>
+template <int HD, bool CAUSAL, bool VT>
 __global__ void __launch_bounds__(kTcThreads, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                         const __grid_constant__ CUtensorMap tm_k,
@@ -74,12 +92,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* q_full = reinterpret_cast<uint64_t*>(smem + L::kBar);
   uint64_t* k_full = q_full + 1;
   uint64_t* v_full = k_full + S;
-  uint64_t* kv_empty = v_full + S;
-  uint64_t* s_full = kv_empty + S;  // [2]: S_X computed
-  uint64_t* p_full = s_full + 2;    // [2]: P_X written (and O_X rescaled), 4 warps arrive
+  uint64_t* kv_empty = v_full + S;  // [2][S]: stage free for tile X (its MMAs completed)
+  uint64_t* s_full = kv_empty + 2 * S;  // [2]: S_X computed
+  uint64_t* s_free = s_full + 2;    // [2]: S_X read into registers (separate P only), 4 warps
+  uint64_t* p_full = s_free + 2;    // [2]: P_X written (and O_X rescaled), 4 warps arrive
   uint64_t* o_done = p_full + 2;    // [2]: O_X += P_X V completed
-  uint64_t* drain = o_done + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* drain = o_done + 2;     // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -107,13 +126,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
       mbar_init(&kv_empty[s], 1);
+      mbar_init(&kv_empty[S + s], 1);
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(&s_full[x], 1);
+      mbar_init(&s_free[x], 4);
       mbar_init(&p_full[x], 4);
       mbar_init(&o_done[x], 1);
     }
-    mbar_init(drain, 1);
+    mbar_init(&drain[0], 1);
+    mbar_init(&drain[1], 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -139,17 +161,28 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       int issued = 0;
       for (int j = 0; j < n_iter; ++j) {
         const int st = j % S;
-        if (j >= S && !mbar_wait(&kv_empty[st], ((j / S) - 1) & 1, err, kDevTimeoutEmpty)) break;
+        if (j >= S) {  // stage st last held tile j - S: wait for the tiles that used it
+          const uint32_t par = ((j / S) - 1) & 1;
+          if (j - S < nA && !mbar_wait(&kv_empty[st], par, err, kDevTimeoutEmpty)) break;
+          if (j - S < nB && !mbar_wait(&kv_empty[S + st], par, err, kDevTimeoutEmpty)) break;
+        }
         mbar_arrive_expect_tx(&k_full[st], L::kTileBytes);
 #pragma unroll
         for (int cb = 0; cb < L::kBlocks; ++cb)
           tma_load_3d(smem + L::kK + st * L::kTileBytes + cb * L::kBlockBytes, &tm_k, &k_full[st],
                       col0 + 64 * cb, j * kTile, b);
         mbar_arrive_expect_tx(&v_full[st], L::kTileBytes);
+        if constexpr (VT) {  // V^T rows h*HD.. (+HD), keys j*128.. in two 64-key boxes
 #pragma unroll
-        for (int cb = 0; cb < L::kBlocks; ++cb)
-          tma_load_3d(smem + L::kV + st * L::kTileBytes + cb * L::kBlockBytes, &tm_v, &v_full[st],
-                      col0 + 64 * cb, j * kTile, b);
+          for (int kb = 0; kb < 2; ++kb)
+            tma_load_3d(smem + L::kV + st * L::kTileBytes + kb * L::kVtBoxBytes, &tm_v,
+                        &v_full[st], j * kTile + 64 * kb, col0, b);
+        } else {
+#pragma unroll
+          for (int cb = 0; cb < L::kBlocks; ++cb)
+            tma_load_3d(smem + L::kV + st * L::kTileBytes + cb * L::kBlockBytes, &tm_v,
+                        &v_full[st], col0 + 64 * cb, j * kTile, b);
+        }
         issued = j + 1;
       }
       // Our own copies land before the CTA may exit (after a timeout nobody
@@ -160,11 +193,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         mbar_wait(&v_full[j % S], (j / S) & 1, nullptr, 0);
       }
     }
-  } else if (warp == 1) {
-    // --------------------------------------------------------- MMA issuer
+  } else if (warp == 1 || warp == 10) {
+    // ------------------------------------------------ MMA issuer of tile x
     if (lane == 0) {
+      const int x = warp == 1 ? 0 : 1;
+      const int nx = x == 0 ? nA : nB;
+      uint64_t* kv_free = kv_empty + x * S;
       constexpr uint32_t id_qk = idesc_f16_f32(kTile, kTile);
-      constexpr uint32_t id_pv = idesc_f16_f32_bmn(kTile, HD);
+      constexpr uint32_t id_pv = VT ? idesc_f16_f32(kTile, HD) : idesc_f16_f32_bmn(kTile, HD);
       const uint32_t sq = smem_u32(smem + L::kQ);
       const uint32_t sk = smem_u32(smem + L::kK);
       const uint32_t sv = smem_u32(smem + L::kV);
@@ -180,72 +216,69 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                      k > 0 ? 1u : 0u);
         }
       };
-      // O_x += P_x V: P from TMEM (16 keys = 8 packed columns per step), V
-      // MN-major (16 keys = 16 rows = 2048 B per step; 64-column blocks of
-      // HD apart by one block).
+      // O_x += P_x V: P from TMEM (16 keys = 8 packed columns per step).
+      // V^T K-major: 16 keys = 32 B inside a 128-byte row, 64 keys per box.
+      // V MN-major: 16 keys = 16 rows = 2048 B; 64-column blocks one block apart.
       auto issue_pv = [&](int x, int st, bool accumulate) {
         const uint32_t b0 = sv + st * L::kTileBytes;
 #pragma unroll
         for (int k = 0; k < kTile / 16; ++k) {
-          mma_f16_ts(tmem + L::kColO + x * HD, tmem + x * kTile + 8 * k,
-                     sdesc_mn_sw128(b0 + k * 2048, L::kBlockBytes), id_pv,
-                     (accumulate || k > 0) ? 1u : 0u);
+          const uint64_t bdesc =
+              VT ? sdesc_k_sw128(b0 + (k >> 2) * L::kVtBoxBytes + (k & 3) * 32)
+                 : sdesc_mn_sw128(b0 + k * 2048, L::kBlockBytes);
+          mma_f16_ts(tmem + L::kColO + x * HD, tmem + L::kColP + x * L::kPStride + 8 * k, bdesc,
+                     id_pv, (accumulate || k > 0) ? 1u : 0u);
         }
       };
       bool ok = mbar_wait(q_full, 0, err, kDevTimeoutFull);
-      if (ok && n_iter > 0) {
+      if (ok && nx > 0) {
         ok = mbar_wait(&k_full[0], 0, err, kDevTimeoutFull);
         if (ok) {
           tc_fence_after();
-          if (nA > 0) {
-            issue_qk(0, 0);
-            mma_commit(&s_full[0]);
-          }
-          if (nB > 0) {
-            issue_qk(1, 0);
-            mma_commit(&s_full[1]);
-          }
+          issue_qk(x, 0);
+          mma_commit(&s_full[x]);
         }
       }
-      for (int j = 0; ok && j < n_iter; ++j) {
+      for (int j = 0; ok && j < nx; ++j) {
         const int st = j % S, st1 = (j + 1) % S;
         const uint32_t par = (j / S) & 1, par1 = ((j + 1) / S) & 1;
         const uint32_t jp = j & 1;
-        if (!mbar_wait(&v_full[st], par, err, kDevTimeoutFull)) break;
-        bool k1 = false;
-        if (j < nA) {
-          if (!mbar_wait(&p_full[0], jp, err, kDevTimeoutOther)) break;
-          tc_fence_after();
-          issue_pv(0, st, j > 0);
-          mma_commit(&o_done[0]);
-          if (j + 1 < nA) {
-            // S_A(j+1) overwrites P_A(j): wait for PV_A(j) to finish reading it.
+        if constexpr (L::kSepP) {
+          // S_X(j) is read early in its softmax, P_X(j) written late: the
+          // next product is queued before this tile's P.V.
+          if (j + 1 < nx) {
             if (!mbar_wait(&k_full[st1], par1, err, kDevTimeoutFull)) break;
-            k1 = true;
-            if (!mbar_wait(&o_done[0], jp, err, kDevTimeoutAccum)) break;
+            if (!mbar_wait(&s_free[x], jp, err, kDevTimeoutOther)) break;
             tc_fence_after();
-            issue_qk(0, st1);
-            mma_commit(&s_full[0]);
+            issue_qk(x, st1);
+            mma_commit(&s_full[x]);
+          }
+          if (!mbar_wait(&v_full[st], par, err, kDevTimeoutFull)) break;
+          if (!mbar_wait(&p_full[x], jp, err, kDevTimeoutOther)) break;
+          tc_fence_after();
+          issue_pv(x, st, j > 0);
+          mma_commit(&o_done[x]);
+          mma_commit(&kv_free[st]);  // K_j and V_j are free for this tile
+        } else {
+          if (!mbar_wait(&v_full[st], par, err, kDevTimeoutFull)) break;
+          if (!mbar_wait(&p_full[x], jp, err, kDevTimeoutOther)) break;
+          tc_fence_after();
+          issue_pv(x, st, j > 0);
+          mma_commit(&o_done[x]);
+          mma_commit(&kv_free[st]);
+          if (j + 1 < nx) {
+            // S_X(j+1) overwrites P_X(j): wait for PV_X(j) to finish reading it.
+            if (!mbar_wait(&k_full[st1], par1, err, kDevTimeoutFull)) break;
+            if (!mbar_wait(&o_done[x], jp, err, kDevTimeoutAccum)) break;
+            tc_fence_after();
+            issue_qk(x, st1);
+            mma_commit(&s_full[x]);
           }
         }
-        if (j < nB) {
-          if (!mbar_wait(&p_full[1], jp, err, kDevTimeoutOther)) break;
-          tc_fence_after();
-          issue_pv(1, st, j > 0);
-          mma_commit(&o_done[1]);
-        }
-        mma_commit(&kv_empty[st]);  // K_j and V_j are free once these MMAs complete
-        if (j + 1 < nB) {
-          if (!k1 && !mbar_wait(&k_full[st1], par1, err, kDevTimeoutFull)) break;
-          if (!mbar_wait(&o_done[1], jp, err, kDevTimeoutAccum)) break;
-          tc_fence_after();
-          issue_qk(1, st1);
-          mma_commit(&s_full[1]);
-        }
       }
-      // Every MMA issued so far completes before TMEM is released.
-      mma_commit(drain);
-      mbar_wait(drain, 0, nullptr, 0);
+      // Every MMA this thread issued completes before TMEM is released.
+      mma_commit(&drain[x]);
+      mbar_wait(&drain[x], 0, nullptr, 0);
     }
   } else {
     // ------------------------------------------------------------ softmax
@@ -257,6 +290,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int nx = x == 0 ? nA : nB;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t t_s = tmem + lane_off + x * kTile;
+    const uint32_t t_p = tmem + lane_off + L::kColP + x * L::kPStride;
     const uint32_t t_o = tmem + lane_off + L::kColO + x * HD;
     const int lim_row = CAUSAL ? min(kend, q + 1) : kend;    // keys [0, lim_row) visible
     const int lim_tile = CAUSAL ? min(kend, qx + 1) : kend;  // smallest lim_row of the tile
@@ -274,6 +308,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       for (int c = 0; c < kTile / 32; ++c)
         tmem_ld32(t_s + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(s + 32 * c));
       tmem_ld_wait();
+      if constexpr (L::kSepP) {  // S_X is in registers: the next S_X may be computed
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[x]);
+      }
       if ((j + 1) * kTile > lim_tile) {  // diagonal or ragged KV tile (warp-uniform)
         const int c0 = lim_row - j * kTile;
 #pragma unroll
@@ -290,40 +329,59 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
       const float m_new = mx * scale_log2;  // -inf when every key of the row is masked
+      bool rescale = false;
+      float f = 1.f;
       if (j == 0) {
         m_ref = mx == -INFINITY ? 0.f : m_new;
       } else if (__any_sync(0xffffffffu, m_new > m_ref + kRescaleLog2)) {
         const float m_up = fmaxf(m_ref, m_new);
-        const float f = fast_exp2(m_ref - m_up);
+        f = fast_exp2(m_ref - m_up);
         m_ref = m_up;
         l0 *= f;
         l1 *= f;
-        // PV(j-1) completed before S(j) was issued, so O is stable here.
-#pragma unroll 1
-        for (int c = 0; c < HD; c += 16) {  // 16 columns at a time: S stays in registers
-          uint32_t o[16];
-          tmem_ld16(t_o + c, o);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
-          tmem_st16(t_o + c, o);
-        }
+        rescale = true;
       }
       const float neg = -m_ref;
+      // P in two halves of 64 keys (32 packed columns each), so S and P never
+      // need registers at the same time.
 #pragma unroll
-      for (int c = 0; c < kTile / 32; ++c) {
-        uint32_t p[16];
+      for (int half = 0; half < 2; ++half) {
+        uint32_t p[32];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float e0 = fast_exp2(fmaf(__uint_as_float(s[32 * c + 2 * i]), scale_log2, neg));
-          const float e1 =
-              fast_exp2(fmaf(__uint_as_float(s[32 * c + 2 * i + 1]), scale_log2, neg));
+        for (int i = 0; i < 32; ++i) {
+          const int c = 64 * half + 2 * i;
+          const float e0 = fast_exp2(fmaf(__uint_as_float(s[c]), scale_log2, neg));
+          const float e1 = fast_exp2(fmaf(__uint_as_float(s[c + 1]), scale_log2, neg));
           l0 += e0;
           l1 += e1;
           p[i] = pack_half2(e0, e1);
         }
-        tmem_st16(t_s + 16 * c, p);
+        if (half == 0) {
+          if constexpr (L::kSepP) {
+            // P_X(j-1) and O_X are read / written by PV_X(j-1) until it completes.
+            if (j > 0 && !__all_sync(0xffffffffu,
+                                     mbar_wait(&o_done[x], (j - 1) & 1, err, kDevTimeoutAccum))) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+          }
+          // (HD 128: PV_X(j-1) completed before S_X(j) was issued.)
+          if (rescale) {
+#pragma unroll 1
+            for (int c = 0; c < HD; c += 16) {
+              uint32_t o[16];
+              tmem_ld16(t_o + c, o);
+              tmem_ld_wait();
+#pragma unroll
+              for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+              tmem_st16(t_o + c, o);
+            }
+          }
+        }
+        tmem_st32(t_p + 32 * half, p);
       }
+      if (!ok) break;
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
@@ -368,25 +426,59 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 }
 
-template <int HD, bool CAUSAL>
-int launch_tc(const __half* q, const __half* k, const __half* v, int64_t ld_qkv, __half* out,
-              int64_t ld_out, int batch, int heads, int seq, float scale,
+// vt[b][c][s] = v[b * seq + s][c] for c < cols, s < seq; zero for seq <= s < ld_vt.
+// 64 tokens x 64 columns per CTA through shared memory; 16-byte loads/stores.
+__global__ void __launch_bounds__(256)
+    transpose_v_kernel(const __half* __restrict__ v, int64_t ld_qkv, __half* __restrict__ vt,
+                       int64_t ld_vt, int seq, int cols) {
+  __shared__ __align__(16) __half tile[64][64 + 8];
+  const int s0 = blockIdx.x * 64, c0 = blockIdx.y * 64, b = blockIdx.z;
+  for (int i = threadIdx.x; i < 64 * 8; i += blockDim.x) {
+    const int r = i >> 3, c = (i & 7) * 8;
+    uint4 val = make_uint4(0, 0, 0, 0);
+    if (s0 + r < seq)
+      val = *reinterpret_cast<const uint4*>(v + (static_cast<int64_t>(b) * seq + s0 + r) * ld_qkv +
+                                            c0 + c);
+    *reinterpret_cast<uint4*>(&tile[r][c]) = val;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 64 * 8; i += blockDim.x) {
+    const int c = i >> 3, s = (i & 7) * 8;
+    if (s0 + s >= ld_vt) continue;
+    __align__(16) __half h8[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) h8[k] = tile[s + k][c];
+    *reinterpret_cast<uint4*>(vt + (static_cast<int64_t>(b) * cols + c0 + c) * ld_vt + s0 + s) =
+        *reinterpret_cast<const uint4*>(h8);
+  }
+}
+
+template <int HD, bool CAUSAL, bool VT>
+int launch_tc(const __half* q, const __half* k, const __half* v, int64_t ld_qkv, int64_t ld_vt,
+              __half* out, int64_t ld_out, int batch, int heads, int seq, float scale,
               const int32_t* valid_len, cudaStream_t stream) {
   using L = TcAttn<HD>;
   static int smem_done[kMaxDevices] = {0};
-  auto kern = attention_tc_kernel<HD, CAUSAL>;
+  auto kern = attention_tc_kernel<HD, CAUSAL, VT>;
   int st = ensure_smem(reinterpret_cast<const void*>(kern), L::kSmem, smem_done);
   if (st != TFX_OK) return st;
   const uint64_t cols = static_cast<uint64_t>(heads) * HD;
   const uint64_t bstride = static_cast<uint64_t>(seq) * static_cast<uint64_t>(ld_qkv);
   CUtensorMap tq, tk, tv;
-  const __half* bases[3] = {q, k, v};
-  CUtensorMap* maps[3] = {&tq, &tk, &tv};
-  for (int i = 0; i < 3; ++i) {
-    st = make_tmap_3d(maps[i], bases[i], static_cast<uint64_t>(seq), static_cast<uint64_t>(batch),
-                      cols, static_cast<uint64_t>(ld_qkv), bstride, 64, kTile);
-    if (st != TFX_OK) return st;
+  st = make_tmap_3d(&tq, q, static_cast<uint64_t>(seq), static_cast<uint64_t>(batch), cols,
+                    static_cast<uint64_t>(ld_qkv), bstride, 64, kTile);
+  if (st == TFX_OK)
+    st = make_tmap_3d(&tk, k, static_cast<uint64_t>(seq), static_cast<uint64_t>(batch), cols,
+                      static_cast<uint64_t>(ld_qkv), bstride, 64, kTile);
+  if (st == TFX_OK) {
+    if (VT)  // [batch][cols][ld_vt]: keys innermost, keys >= seq read as zeros
+      st = make_tmap_3d(&tv, v, cols, static_cast<uint64_t>(batch), static_cast<uint64_t>(seq),
+                        static_cast<uint64_t>(ld_vt), cols * static_cast<uint64_t>(ld_vt), 64, HD);
+    else
+      st = make_tmap_3d(&tv, v, static_cast<uint64_t>(seq), static_cast<uint64_t>(batch), cols,
+                        static_cast<uint64_t>(ld_qkv), bstride, 64, kTile);
   }
+  if (st != TFX_OK) return st;
   const int nqb = (seq + 2 * kTile - 1) / (2 * kTile);
   const dim3 grid(static_cast<unsigned>(batch) * static_cast<unsigned>(heads),
                   static_cast<unsigned>(nqb));
@@ -394,6 +486,26 @@ int launch_tc(const __half* q, const __half* k, const __half* v, int64_t ld_qkv,
                                                 scale * 1.4426950408889634f, valid_len,
                                                 device_error_word());
   return check_launch("attention_tc_kernel");
+}
+
+template <bool VT>
+int dispatch_tc(const __half* q, const __half* k, const __half* v, int64_t ld_qkv, int64_t ld_vt,
+                __half* out, int64_t ld_out, int batch, int heads, int seq, int head_dim,
+                float scale, int causal, const int32_t* valid_len, cudaStream_t stream) {
+  if (static_cast<int64_t>(batch) * heads > 0x7fffffff ||
+      (seq + 2 * kTile - 1) / (2 * kTile) > 65535)
+    return fail(TFX_ERR_UNSUPPORTED, "tfx_attention: batch*heads or seq too large for the grid");
+  if (head_dim == 64)
+    return causal ? launch_tc<64, true, VT>(q, k, v, ld_qkv, ld_vt, out, ld_out, batch, heads,
+                                            seq, scale, valid_len, stream)
+                  : launch_tc<64, false, VT>(q, k, v, ld_qkv, ld_vt, out, ld_out, batch, heads,
+                                             seq, scale, valid_len, stream);
+  if (head_dim == 128)
+    return causal ? launch_tc<128, true, VT>(q, k, v, ld_qkv, ld_vt, out, ld_out, batch, heads,
+                                             seq, scale, valid_len, stream)
+                  : launch_tc<128, false, VT>(q, k, v, ld_qkv, ld_vt, out, ld_out, batch, heads,
+                                              seq, scale, valid_len, stream);
+  return fail(TFX_ERR_UNSUPPORTED, "attention_tc: head_dim %d not in {64,128}", head_dim);
 }
 
 }  // namespace
@@ -405,19 +517,27 @@ bool attention_tc_supported(int head_dim, float scale) {
 int launch_attention_tc(const __half* q, const __half* k, const __half* v, int64_t ld_qkv,
                         __half* out, int64_t ld_out, int batch, int heads, int seq, int head_dim,
                         float scale, int causal, const int32_t* valid_len, cudaStream_t stream) {
-  if (static_cast<int64_t>(batch) * heads > 0x7fffffff || (seq + 2 * kTile - 1) / (2 * kTile) > 65535)
-    return fail(TFX_ERR_UNSUPPORTED, "tfx_attention: batch*heads or seq too large for the grid");
-  if (head_dim == 64)
-    return causal ? launch_tc<64, true>(q, k, v, ld_qkv, out, ld_out, batch, heads, seq, scale,
-                                        valid_len, stream)
-                  : launch_tc<64, false>(q, k, v, ld_qkv, out, ld_out, batch, heads, seq, scale,
-                                         valid_len, stream);
-  if (head_dim == 128)
-    return causal ? launch_tc<128, true>(q, k, v, ld_qkv, out, ld_out, batch, heads, seq, scale,
-                                         valid_len, stream)
-                  : launch_tc<128, false>(q, k, v, ld_qkv, out, ld_out, batch, heads, seq, scale,
-                                          valid_len, stream);
-  return fail(TFX_ERR_UNSUPPORTED, "attention_tc: head_dim %d not in {64,128}", head_dim);
+  return dispatch_tc<false>(q, k, v, ld_qkv, 0, out, ld_out, batch, heads, seq, head_dim, scale,
+                            causal, valid_len, stream);
+}
+
+int64_t attention_vt_ld(int seq) { return (static_cast<int64_t>(seq) + 7) / 8 * 8; }
+
+int launch_transpose_v(const __half* v, int64_t ld_qkv, __half* vt, int batch, int seq,
+                       int cols, cudaStream_t stream) {
+  const int64_t ld_vt = attention_vt_ld(seq);
+  const dim3 grid(static_cast<unsigned>((ld_vt + 63) / 64), static_cast<unsigned>(cols / 64),
+                  static_cast<unsigned>(batch));
+  transpose_v_kernel<<<grid, 256, 0, stream>>>(v, ld_qkv, vt, ld_vt, seq, cols);
+  return check_launch("transpose_v_kernel");
+}
+
+int launch_attention_tc_vt(const __half* q, const __half* k, const __half* vt, int64_t ld_qkv,
+                           __half* out, int64_t ld_out, int batch, int heads, int seq,
+                           int head_dim, float scale, int causal, const int32_t* valid_len,
+                           cudaStream_t stream) {
+  return dispatch_tc<true>(q, k, vt, ld_qkv, attention_vt_ld(seq), out, ld_out, batch, heads,
+                           seq, head_dim, scale, causal, valid_len, stream);
 }
 
 }  // namespace tfx

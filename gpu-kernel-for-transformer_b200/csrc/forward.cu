@@ -6,6 +6,7 @@
 //   h   = LN(x; layers[0].norm1)                              [fp16]
 //   per layer l:
 //     qkv = h . Wqkv^T + bqkv                                 [fp16, tcgen05]
+//     (head_dim 64/128: V^T = transpose(V) into h's buffer)   [fp16]
 //     ctx = attention(qkv)                                    [fp16]
 //     r   = ctx . Wo^T + bo + (l == 0 ? x : r)                [fp32, tcgen05]
 //     h   = LN(r; norm2)                                      [fp16]
@@ -50,7 +51,11 @@ struct Workspace {
   size_t bytes;
 };
 
-Workspace plan_workspace(char* base, int64_t m, int d, int f) {
+// The tcgen05 attention path (head_dim 64/128) reads V transposed; the copy
+// lives in h's buffer, which is dead between the QKV GEMM and LayerNorm 2.
+bool attention_reads_vt(int hd) { return attention_tc_supported(hd, 1.0f); }
+
+Workspace plan_workspace(char* base, int batch, int seq, int d, int f, int hd) {
   Workspace w{};
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -58,7 +63,13 @@ Workspace plan_workspace(char* base, int64_t m, int d, int f) {
     off += round_up(bytes);
     return p;
   };
-  w.h = reinterpret_cast<__half*>(take(sizeof(__half) * m * d));
+  const int64_t m = static_cast<int64_t>(batch) * seq;
+  size_t h_bytes = sizeof(__half) * m * d;
+  if (attention_reads_vt(hd)) {
+    const size_t vt_bytes = sizeof(__half) * static_cast<size_t>(batch) * d * attention_vt_ld(seq);
+    h_bytes = h_bytes > vt_bytes ? h_bytes : vt_bytes;
+  }
+  w.h = reinterpret_cast<__half*>(take(h_bytes));
   w.qkv = reinterpret_cast<__half*>(take(sizeof(__half) * m * 3 * d));
   w.ctx = reinterpret_cast<__half*>(take(sizeof(__half) * m * d));
   w.res = reinterpret_cast<float*>(take(sizeof(float) * m * d));
@@ -108,8 +119,9 @@ int tfx_set_fused_policy(int enable) {
 int64_t tfx_forward_workspace_bytes(const tfx_model* model, int batch, int seq) {
   if (check_model(model) != TFX_OK || batch <= 0 || seq <= 0) return -1;
   if (use_fused(model, seq, nullptr)) return 0;
-  const int64_t m = static_cast<int64_t>(batch) * seq;
-  return static_cast<int64_t>(plan_workspace(nullptr, m, model->d_model, model->ffn_dim).bytes);
+  return static_cast<int64_t>(plan_workspace(nullptr, batch, seq, model->d_model, model->ffn_dim,
+                                            model->d_model / model->num_heads)
+                                 .bytes);
 }
 
 int tfx_forward(const tfx_model* model, const float* x, float* y, int batch, int seq,
@@ -132,7 +144,7 @@ int tfx_forward(const tfx_model* model, const float* x, float* y, int batch, int
     return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward: null workspace");
   const int64_t m = static_cast<int64_t>(batch) * seq;
   const int d = model->d_model, f = model->ffn_dim, nh = model->num_heads, hd = d / nh;
-  const Workspace ws = plan_workspace(static_cast<char*>(workspace), m, d, f);
+  const Workspace ws = plan_workspace(static_cast<char*>(workspace), batch, seq, d, f, hd);
   if (workspace_bytes < ws.bytes)
     return fail(TFX_ERR_WORKSPACE, "tfx_forward: workspace %zu < required %zu bytes",
                 workspace_bytes, ws.bytes);
@@ -149,8 +161,15 @@ int tfx_forward(const tfx_model* model, const float* x, float* y, int batch, int
     st = launch_linear(ws.h, d, wqkv, L.qkv_bias, nullptr, 0, ws.qkv, 3 * d, m, 3 * d, d,
                        TFX_EPI_BIAS, stream);
     if (st != TFX_OK) return st;
-    st = launch_attention(ws.qkv, ws.qkv + d, ws.qkv + 2 * d, 3 * d, ws.ctx, d, batch, nh, seq,
-                          hd, scale, model->causal, valid_len, stream);
+    if (attention_reads_vt(hd)) {
+      st = launch_transpose_v(ws.qkv + 2 * d, 3 * d, ws.h, batch, seq, d, stream);
+      if (st != TFX_OK) return st;
+      st = launch_attention_tc_vt(ws.qkv, ws.qkv + d, ws.h, 3 * d, ws.ctx, d, batch, nh, seq, hd,
+                                  scale, model->causal, valid_len, stream);
+    } else {
+      st = launch_attention(ws.qkv, ws.qkv + d, ws.qkv + 2 * d, 3 * d, ws.ctx, d, batch, nh, seq,
+                            hd, scale, model->causal, valid_len, stream);
+    }
     if (st != TFX_OK) return st;
     st = launch_linear(ws.ctx, d, reinterpret_cast<const __half*>(L.out_weight), L.out_bias,
                        l == 0 ? x : ws.res, d, ws.res, d, m, d, d, TFX_EPI_BIAS_RESIDUAL, stream);

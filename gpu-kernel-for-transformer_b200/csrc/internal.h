@@ -62,6 +62,16 @@ bool attention_tc_supported(int head_dim, float scale);
 int launch_attention_tc(const __half* q, const __half* k, const __half* v, int64_t ld_qkv,
                         __half* out, int64_t ld_out, int batch, int heads, int seq, int head_dim,
                         float scale, int causal, const int32_t* valid_len, cudaStream_t stream);
+// Same kernel reading V from a transposed copy vt[b][h*hd + d][s] (row pitch
+// attention_vt_ld(seq) elements), written by launch_transpose_v from the
+// packed projection; the P.V products then use a K-major operand.
+int64_t attention_vt_ld(int seq);
+int launch_transpose_v(const __half* v, int64_t ld_qkv, __half* vt, int batch, int seq, int cols,
+                       cudaStream_t stream);
+int launch_attention_tc_vt(const __half* q, const __half* k, const __half* vt, int64_t ld_qkv,
+                           __half* out, int64_t ld_out, int batch, int heads, int seq,
+                           int head_dim, float scale, int causal, const int32_t* valid_len,
+                           cudaStream_t stream);
 
 // Whole-forward fused kernel (d_model = ffn_dim = 128, seq | 128).
 bool fused_forward_supported(const tfx_model* m, int seq, const int32_t* valid_len);

@@ -112,3 +112,26 @@ def test_workspace_size_formula(lib):
     assert need == rows * per_row
     # seq not dividing 128: the per-op chain and its workspace
     assert lib.tfx_forward_workspace_bytes(ctypes.byref(m), 10, 100) == 1000 * per_row
+
+
+def test_workspace_holds_transposed_v_for_tcgen05_attention(lib):
+    """head_dim 64: the h buffer also holds V^T [B][D][S rounded up to 8]."""
+    pkg = load_package()
+    L = pkg._lib
+    m = L.TfxModel()
+    m.d_model, m.num_heads, m.ffn_dim, m.num_layers = 256, 4, 512, 1
+    layers = (L.TfxLayer * 1)()
+    for f, _ in L.TfxLayer._fields_:
+        setattr(layers[0], f, 256)
+    m.layers = ctypes.cast(layers, ctypes.POINTER(L.TfxLayer))
+    m.final_norm_weight = m.final_norm_bias = 256
+
+    def up(n):
+        return (n + 255) // 256 * 256
+
+    b, s, d, f = 3, 261, 256, 512
+    rows = b * s
+    vt = 2 * b * d * ((s + 7) // 8 * 8)
+    expect = up(max(2 * rows * d, vt)) + up(2 * rows * 3 * d) + up(2 * rows * d) + \
+        up(4 * rows * d) + up(2 * rows * f)
+    assert lib.tfx_forward_workspace_bytes(ctypes.byref(m), b, s) == expect

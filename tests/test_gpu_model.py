@@ -97,6 +97,26 @@ def test_c5_prefix_of_full_length_sequence(pkg, dev):
     assert res.failed_elements == 0, (res.failed_elements, res.max_abs_error)
 
 
+@pytest.mark.parametrize("cfg", [
+    # head_dim 128, ragged length, causal, padded batch
+    dict(batch_size=3, seq_len=300, d_model=256, num_heads=2, ffn_dim=512, num_layers=2,
+         causal=True),
+    # head_dim 64, non-causal, length not a multiple of 8 (V^T row padding)
+    dict(batch_size=2, seq_len=261, d_model=256, num_heads=4, ffn_dim=256, num_layers=2,
+         causal=False),
+])
+def test_tcgen05_attention_head_dims_padded(pkg, dev, cfg):
+    """head_dim 64/128 run the tcgen05 attention on a transposed V; padding
+    masks keys past each sequence's length."""
+    oracle_model, cand = _pair(pkg, cfg, 4321, dev)
+    x, mask = ob.generate_random_case(ob.TransformerConfig(**cfg), 99, 0.3)
+    with torch.inference_mode():
+        ref = oracle_model(x, mask)
+        y = cand(x.to(dev), mask.to(dev)).cpu()
+    res = ob.compare_outputs(ref, y, RTOL, ATOL)
+    assert res.failed_elements == 0, (res.failed_elements, res.max_abs_error)
+
+
 def test_graph_replay_matches_eager(pkg, dev):
     cfg = dict(batch_size=4, seq_len=128, d_model=128, num_heads=4, ffn_dim=128,
                num_layers=4, causal=True)
