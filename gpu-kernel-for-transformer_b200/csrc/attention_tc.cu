@@ -55,6 +55,13 @@ namespace {
 constexpr int kTcThreads = 352;
 constexpr int kTile = 128;            // query rows per tile = keys per KV tile
 constexpr float kRescaleLog2 = 8.0f;  // lazy-rescale threshold (P <= 2^8)
+// Of every 8 pairs of scores, this many take 2^x from the FMA-pipe polynomial
+// (exp2_poly_f2) and the rest from the MUFU unit (16 results per clock per
+// SM), which alone bounds the softmax at head_dim 64.
+#ifndef TFX_ATTN_POLY_OF8
+#define TFX_ATTN_POLY_OF8 2
+#endif
+constexpr int kPolyOf8 = TFX_ATTN_POLY_OF8;
 constexpr uint32_t kTmemCols = 512;
 
 template <int HD>
@@ -201,31 +208,33 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       uint64_t* kv_free = kv_empty + x * S;
       constexpr uint32_t id_qk = idesc_f16_f32(kTile, kTile);
       constexpr uint32_t id_pv = VT ? idesc_f16_f32(kTile, HD) : idesc_f16_f32_bmn(kTile, HD);
-      const uint32_t sq = smem_u32(smem + L::kQ);
-      const uint32_t sk = smem_u32(smem + L::kK);
-      const uint32_t sv = smem_u32(smem + L::kV);
+      // Descriptors are built once; each MMA adds a constant to the 64-bit
+      // value (address field in 16-byte units, bits 0-13; shared addresses
+      // stay below 2^18 so the field never carries into the next one).
+      const uint64_t dq0 = sdesc_k_sw128(smem_u32(smem + L::kQ));
+      const uint64_t dk0 = sdesc_k_sw128(smem_u32(smem + L::kK));
+      const uint64_t dv0 = VT ? sdesc_k_sw128(smem_u32(smem + L::kV))
+                              : sdesc_mn_sw128(smem_u32(smem + L::kV), L::kBlockBytes);
       // S_x = Q_x K^T: both operands K-major; K advances 16 columns = 32 B
       // inside a 128-byte swizzled row, then to the next 64-column block.
       auto issue_qk = [&](int x, int st) {
-        const uint32_t a0 = sq + x * L::kTileBytes;
-        const uint32_t b0 = sk + st * L::kTileBytes;
+        const uint64_t da = dq0 + static_cast<uint64_t>(x * (L::kTileBytes >> 4));
+        const uint64_t db = dk0 + static_cast<uint64_t>(st * (L::kTileBytes >> 4));
 #pragma unroll
         for (int k = 0; k < HD / 16; ++k) {
-          const uint32_t off = (k >> 2) * L::kBlockBytes + (k & 3) * 32;
-          mma_f16_ss(tmem + x * kTile, sdesc_k_sw128(a0 + off), sdesc_k_sw128(b0 + off), id_qk,
-                     k > 0 ? 1u : 0u);
+          const uint64_t off = static_cast<uint64_t>(((k >> 2) * L::kBlockBytes + (k & 3) * 32) >> 4);
+          mma_f16_ss(tmem + x * kTile, da + off, db + off, id_qk, k > 0 ? 1u : 0u);
         }
       };
       // O_x += P_x V: P from TMEM (16 keys = 8 packed columns per step).
       // V^T K-major: 16 keys = 32 B inside a 128-byte row, 64 keys per box.
       // V MN-major: 16 keys = 16 rows = 2048 B; 64-column blocks one block apart.
       auto issue_pv = [&](int x, int st, bool accumulate) {
-        const uint32_t b0 = sv + st * L::kTileBytes;
+        const uint64_t db = dv0 + static_cast<uint64_t>(st * (L::kTileBytes >> 4));
 #pragma unroll
         for (int k = 0; k < kTile / 16; ++k) {
-          const uint64_t bdesc =
-              VT ? sdesc_k_sw128(b0 + (k >> 2) * L::kVtBoxBytes + (k & 3) * 32)
-                 : sdesc_mn_sw128(b0 + k * 2048, L::kBlockBytes);
+          const uint64_t bdesc = db + static_cast<uint64_t>(
+              (VT ? (k >> 2) * L::kVtBoxBytes + (k & 3) * 32 : k * 2048) >> 4);
           mma_f16_ts(tmem + L::kColO + x * HD, tmem + L::kColP + x * L::kPStride + 8 * k, bdesc,
                      id_pv, (accumulate || k > 0) ? 1u : 0u);
         }
@@ -295,7 +304,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int lim_row = CAUSAL ? min(kend, q + 1) : kend;    // keys [0, lim_row) visible
     const int lim_tile = CAUSAL ? min(kend, qx + 1) : kend;  // smallest lim_row of the tile
     float m_ref = 0.f;
-    float l0 = 0.f, l1 = 0.f;
+    uint64_t lsum0 = 0, lsum1 = 0;
     bool ok = true;
     for (int j = 0; j < nx; ++j) {
       if (!__all_sync(0xffffffffu, mbar_wait(&s_full[x], j & 1, err, kDevTimeoutAccum))) {
@@ -319,15 +328,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int c = 0; c < kTile; ++c)
           if (c >= c0) s[c] = 0xff800000u;  // -inf
       }
-      float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+      float mm[8];
 #pragma unroll
-      for (int c = 0; c < kTile; c += 4) {
-        mx0 = fmaxf(mx0, __uint_as_float(s[c]));
-        mx1 = fmaxf(mx1, __uint_as_float(s[c + 1]));
-        mx2 = fmaxf(mx2, __uint_as_float(s[c + 2]));
-        mx3 = fmaxf(mx3, __uint_as_float(s[c + 3]));
-      }
-      const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+      for (int i = 0; i < 8; ++i) mm[i] = fmaxf(__uint_as_float(s[i]), __uint_as_float(s[i + 8]));
+#pragma unroll
+      for (int c = 16; c < kTile; c += 16)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mm[i] = fmax3(mm[i], __uint_as_float(s[c + i]), __uint_as_float(s[c + 8 + i]));
+      const float mx = fmaxf(fmax3(mm[0], mm[1], mm[2]), fmax3(fmax3(mm[3], mm[4], mm[5]), mm[6], mm[7]));
       const float m_new = mx * scale_log2;  // -inf when every key of the row is masked
       bool rescale = false;
       float f = 1.f;
@@ -337,11 +345,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const float m_up = fmaxf(m_ref, m_new);
         f = fast_exp2(m_ref - m_up);
         m_ref = m_up;
-        l0 *= f;
-        l1 *= f;
+        const uint64_t f2v = f2_pack(f, f);
+        lsum0 = f2_fma(lsum0, f2v, 0);
+        lsum1 = f2_fma(lsum1, f2v, 0);
         rescale = true;
       }
-      const float neg = -m_ref;
+      const uint64_t c2 = f2_pack(scale_log2, scale_log2);
+      const uint64_t negm2 = f2_pack(-m_ref, -m_ref);
       // P in two halves of 64 keys (32 packed columns each), so S and P never
       // need registers at the same time.
 #pragma unroll
@@ -350,10 +360,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const int c = 64 * half + 2 * i;
-          const float e0 = fast_exp2(fmaf(__uint_as_float(s[c]), scale_log2, neg));
-          const float e1 = fast_exp2(fmaf(__uint_as_float(s[c + 1]), scale_log2, neg));
-          l0 += e0;
-          l1 += e1;
+          const uint64_t arg = f2_fma(f2_pack(__uint_as_float(s[c]), __uint_as_float(s[c + 1])), c2, negm2);
+          uint64_t e;
+          if ((i & 7) < kPolyOf8) {
+            e = exp2_poly_f2(arg);
+          } else {
+            float a0, a1;
+            f2_unpack(arg, a0, a1);
+            e = f2_pack(fast_exp2(a0), fast_exp2(a1));
+          }
+          if (i & 1) lsum1 = f2_add(lsum1, e); else lsum0 = f2_add(lsum0, e);
+          float e0, e1;
+          f2_unpack(e, e0, e1);
           p[i] = pack_half2(e0, e1);
         }
         if (half == 0) {
@@ -389,7 +407,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     if (ok && nx > 0)
       ok = __all_sync(0xffffffffu, mbar_wait(&o_done[x], (nx - 1) & 1, err, kDevTimeoutAccum));
-    const float l = l0 + l1;
+    float la, lb, lc, ld;
+    f2_unpack(lsum0, la, lb);
+    f2_unpack(lsum1, lc, ld);
+    const float l = (la + lb) + (lc + ld);
     const float inv = l > 0.f ? 1.f / l : 0.f;
     __half* dst = out + (static_cast<int64_t>(b) * seq + q) * ld_out + h * HD;
     if (ok && nx > 0) {

@@ -109,6 +109,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1 && lane == 0) {
     // --------------------------------------------------------- MMA issuer
     constexpr uint32_t idesc = idesc_f16_f32(kBM, BN);
+    // Descriptors built once; per stage and k-step a constant is added to the
+    // 64-bit value (address field in 16-byte units, no carry below 2^18 B).
+    const uint64_t da0 = sdesc_k_sw128(smem_u32(smem));
+    const uint64_t db0 = sdesc_k_sw128(smem_u32(smem + L::kABytes));
     int stage = 0;
     uint32_t phase = 0;
     int local = 0;
@@ -125,12 +129,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t a_addr = smem_u32(smem + stage * L::kStageBytes);
-        const uint32_t b_addr = a_addr + L::kABytes;
+        const uint64_t soff = static_cast<uint64_t>(stage * (L::kStageBytes >> 4));
 #pragma unroll
         for (int k = 0; k < kBK / 16; ++k) {
-          mma_f16_ss(d_tmem, sdesc_k_sw128(a_addr + k * 32), sdesc_k_sw128(b_addr + k * 32),
-                     idesc, (kb | k) != 0 ? 1u : 0u);
+          mma_f16_ss(d_tmem, da0 + soff + 2 * k, db0 + soff + 2 * k, idesc,
+                     (kb | k) != 0 ? 1u : 0u);
         }
         mma_commit(&empty[stage]);
         if (++stage == STAGES) {

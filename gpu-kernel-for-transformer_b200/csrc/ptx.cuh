@@ -364,7 +364,75 @@ __device__ __forceinline__ float gelu_as(float x) {
   return x * (x >= 0.f ? 1.0f - half_tail : half_tail);
 }
 
+// ------------------------------------------------- packed fp32 pairs (sm_100)
+// Two fp32 values in one 64-bit register pair; add/sub/fma.rn.f32x2 do both
+// lanes in one instruction (half the issue slots of scalar FADD/FFMA).
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
+// max(a, b, c) in one instruction (sm_100 three-input max).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^x for a pair, on the FMA pipe instead of the MUFU unit. Cody-Waite range
+// reduction x = n + f with n = round(x) (the 1.5 * 2^23 rounding-constant
+// trick, exact in round-to-nearest for |x| < 2^22) and |f| <= 1/2; 2^f from a
+// degree-3 polynomial whose coefficients are a relative-error minimax fit on
+// [-1/2, 1/2] computed for this file (Lawson's iteratively reweighted least
+// squares; max relative error 7.5e-5, below half an fp16 ulp, 2.4e-4); 2^n is
+// applied by adding n to the exponent field. Inputs are clamped to >= -126 so
+// the exponent never underflows (results below 2^-126 only feed fp16 P
+// values, where they round to 0); -inf gives 2^-126. Inputs must be <= 127.
+__device__ __forceinline__ uint64_t exp2_poly_f2(uint64_t x) {
+  float x0, x1;
+  f2_unpack(x, x0, x1);
+  const uint64_t xc = f2_pack(fmaxf(x0, -126.0f), fmaxf(x1, -126.0f));
+  const uint64_t kRound = f2_pack(12582912.0f, 12582912.0f);  // 1.5 * 2^23
+  const uint64_t j = f2_add(xc, kRound);                        // n in the low mantissa bits
+  const uint64_t f = f2_sub(xc, f2_sub(j, kRound));             // x - n
+  uint64_t p = f2_fma(f, f2_pack(0.055171433836221695f, 0.055171433836221695f),
+                      f2_pack(0.24261081218719482f, 0.24261081218719482f));
+  p = f2_fma(p, f, f2_pack(0.6932609677314758f, 0.6932609677314758f));
+  p = f2_fma(p, f, f2_pack(0.9999281167984009f, 0.9999281167984009f));
+  float p0, p1, j0, j1;
+  f2_unpack(p, p0, p1);
+  f2_unpack(j, j0, j1);
+  const uint32_t r0 = __float_as_uint(p0) + (__float_as_uint(j0) << 23);
+  const uint32_t r1 = __float_as_uint(p1) + (__float_as_uint(j1) << 23);
+  return f2_pack(__uint_as_float(r0), __uint_as_float(r1));
+}
+
 // Named barrier over `count` threads (a multiple of 32) with id `id` (1..15).
+// Arrive on named barrier `id` without waiting (pairs with named_bar_sync
+// by the other threads of the `count`).
+__device__ __forceinline__ void named_bar_arrive(int id, int count) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
