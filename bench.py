@@ -76,6 +76,8 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the per-GPU batch (small cases for ncu captures only)")
+    ap.add_argument("--seq", type=int, default=None,
+                    help="override the sequence length (small cases for ncu captures only)")
     ap.add_argument("--chain", action="store_true",
                     help="force the per-op kernel chain instead of the fused kernel")
     return ap.parse_args()
@@ -283,12 +285,15 @@ def kernel_breakdown(pkg, model, x, ws, steps):
     hd = D // Hh
     eps = mdl.eps
 
-    # Same workspace layout as tfx_forward (csrc/forward.cu plan_workspace).
+    # Same workspace layout as tfx_forward (csrc/forward.cu plan_workspace):
+    # for head_dim 64/128 the h buffer also holds V transposed.
     def carve(nbytes, off):
         return ws.data_ptr() + off, off + (nbytes + 255) // 256 * 256
 
+    vt_path = hd in (64, 128)
+    ld_vt = lib.tfx_attention_vt_ld(S)
     off = 0
-    h, off = carve(2 * M * D, off)
+    h, off = carve(max(2 * M * D, 2 * B * D * ld_vt) if vt_path else 2 * M * D, off)
     qkv, off = carve(2 * M * 3 * D, off)
     ctx, off = carve(2 * M * D, off)
     res, off = carve(4 * M * D, off)
@@ -313,9 +318,16 @@ def kernel_breakdown(pkg, model, x, ws, steps):
             Ly = layers[li]
             timed("gemm_qkv", lambda: lib.tfx_linear(h, Ly.qkv_weight, Ly.qkv_bias, None, qkv,
                                                      M, 3 * D, D, 0, stream))
-            timed("attention", lambda: lib.tfx_attention(
-                qkv, qkv + 2 * D, qkv + 4 * D, 3 * D, ctx, D, B, Hh, S, hd, hd ** -0.5, 1,
-                None, stream))
+            if vt_path:
+                timed("transpose_v", lambda: lib.tfx_transpose_v(qkv + 4 * D, 3 * D, h, B, S, D,
+                                                                 stream))
+                timed("attention", lambda: lib.tfx_attention_vt(
+                    qkv, qkv + 2 * D, h, 3 * D, ctx, D, B, Hh, S, hd, hd ** -0.5, 1, None,
+                    stream))
+            else:
+                timed("attention", lambda: lib.tfx_attention(
+                    qkv, qkv + 2 * D, qkv + 4 * D, 3 * D, ctx, D, B, Hh, S, hd, hd ** -0.5, 1,
+                    None, stream))
             timed("gemm_out_residual", lambda: lib.tfx_linear(
                 ctx, Ly.out_weight, Ly.out_bias, x.data_ptr() if li == 0 else res, res, M, D, D,
                 2, stream))
@@ -339,6 +351,7 @@ def algorithmic(kind, M, S, D, H, F):
         "layernorm": (M * D * (4 + 2), 0),
         "gemm_qkv": (M * D * 2 + M * 3 * D * 2 + 3 * D * D * 2, 2 * M * D * 3 * D),
         "attention": (M * 3 * D * 2 + M * D * 2, 2 * M * D * (S + 1)),
+        "transpose_v": (M * D * 2 * 2, 0),
         "gemm_out_residual": (M * D * 2 + M * D * 4 * 2 + D * D * 2, 2 * M * D * D),
         "gemm_ffn_in_gelu": (M * D * 2 + M * F * 2 + F * D * 2, 2 * M * D * F),
         "gemm_ffn_out_residual": (M * F * 2 + M * D * 4 * 2 + D * F * 2, 2 * M * D * F),
@@ -370,6 +383,8 @@ def main():
     B, S, D, H, F, L = CONFIGS[args.config]
     if args.batch:
         B = args.batch
+    if args.seq:
+        S = args.seq
     cfg = pkg.TransformerConfig(B, S, D, H, F, L, True)
     torch.manual_seed(SEED)
     model = pkg.UserOptimizedTransformer(cfg).to(dev).eval()
@@ -412,7 +427,10 @@ def main():
     ms_per_step = ms_total / args.steps
     tokens_per_step = world * B * S
     value = tokens_per_step / (ms_per_step / 1e3)
-    launches_per_forward = 1 if fused else 7 * L + 1
+    # Per-op chain: LN, then per layer QKV GEMM, [V transpose,] attention,
+    # out-proj, LN, FFN-in, FFN-out, LN.
+    vt_path = (D // H) in (64, 128)
+    launches_per_forward = 1 if fused else (8 if vt_path else 7) * L + 1
 
     # ---- e2e: public API with host buffers (H2D of x, forward, D2H of y)
     e2e = None

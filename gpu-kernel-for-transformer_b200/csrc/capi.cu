@@ -249,6 +249,51 @@ int tfx_attention(const tfx_half* q, const tfx_half* k, const tfx_half* v, int64
                           scale, causal, valid_len, reinterpret_cast<cudaStream_t>(stream));
 }
 
+int64_t tfx_attention_vt_ld(int seq) { return seq > 0 ? attention_vt_ld(seq) : -1; }
+
+int tfx_transpose_v(const tfx_half* v, int64_t ld_qkv, tfx_half* vt, int batch, int seq, int cols,
+                    tfx_stream_t stream) {
+  g_msg[0] = 0;
+  if (v == nullptr || vt == nullptr) return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_transpose_v: null tensor");
+  if (batch <= 0 || seq <= 0 || cols <= 0 || ld_qkv < cols)
+    return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_transpose_v: bad sizes");
+  if (cols % 64 != 0 || batch > 65535 || (cols / 64) > 65535)
+    return fail(TFX_ERR_UNSUPPORTED, "tfx_transpose_v: cols must be a multiple of 64");
+  if (!aligned(v, 16) || !aligned(vt, 16) || ld_qkv % 8 != 0)
+    return fail(TFX_ERR_MISALIGNED, "tfx_transpose_v: 16-byte aligned pointers, ld_qkv %% 8 == 0");
+  return launch_transpose_v(reinterpret_cast<const __half*>(v), ld_qkv,
+                            reinterpret_cast<__half*>(vt), batch, seq, cols,
+                            reinterpret_cast<cudaStream_t>(stream));
+}
+
+int tfx_attention_vt(const tfx_half* q, const tfx_half* k, const tfx_half* vt, int64_t ld_qkv,
+                     tfx_half* out, int64_t ld_out, int batch, int heads, int seq, int head_dim,
+                     float scale, int causal, const int32_t* valid_len, tfx_stream_t stream) {
+  g_msg[0] = 0;
+  if (q == nullptr || k == nullptr || vt == nullptr || out == nullptr)
+    return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_attention_vt: null tensor");
+  if (batch <= 0 || heads <= 0 || seq <= 0 || head_dim <= 0)
+    return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_attention_vt: sizes must be positive");
+  if (!attention_tc_supported(head_dim, scale))
+    return fail(TFX_ERR_UNSUPPORTED, "tfx_attention_vt: head_dim %d not in {64,128} or scale <= 0",
+                head_dim);
+  if (heads > 65535 || batch > 65535)
+    return fail(TFX_ERR_UNSUPPORTED, "tfx_attention_vt: batch and heads must be <= 65535");
+  if (ld_qkv < static_cast<int64_t>(heads) * head_dim ||
+      ld_out < static_cast<int64_t>(heads) * head_dim)
+    return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_attention_vt: leading dimension smaller than H*hd");
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(vt, 16) || !aligned(out, 16) ||
+      ld_qkv % 8 != 0 || ld_out % 8 != 0)
+    return fail(TFX_ERR_MISALIGNED,
+                "tfx_attention_vt: pointers 16-byte aligned and leading dims multiples of 8 needed");
+  return launch_attention_tc_vt(reinterpret_cast<const __half*>(q),
+                                reinterpret_cast<const __half*>(k),
+                                reinterpret_cast<const __half*>(vt), ld_qkv,
+                                reinterpret_cast<__half*>(out), ld_out, batch, heads, seq,
+                                head_dim, scale, causal, valid_len,
+                                reinterpret_cast<cudaStream_t>(stream));
+}
+
 int tfx_read_device_error(int* code) {
   g_msg[0] = 0;
   if (code == nullptr) return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_read_device_error: null code");

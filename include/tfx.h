@@ -117,6 +117,27 @@ TFX_API int tfx_attention(const tfx_half* q, const tfx_half* k, const tfx_half* 
                   tfx_half* out, int64_t ld_out, int batch, int heads, int seq, int head_dim,
                   float scale, int causal, const int32_t* valid_len, tfx_stream_t stream);
 
+/*
+ * The attention path tfx_forward takes for head_dim 64 and 128, in its two
+ * steps. No counterpart in the reference: V transposed is this library's
+ * internal layout (the tcgen05 P.V products then read V as a K-major operand
+ * at full rate); exported so the per-kernel benchmark and the parity tests can
+ * drive exactly what the forward runs.
+ *
+ * tfx_transpose_v: vt[b][c][s] = v[(b*seq + s)*ld_qkv + c] for c < cols
+ * (cols = H*head_dim, a multiple of 64), s < seq; row pitch
+ * tfx_attention_vt_ld(seq) elements (seq rounded up to 8), zero-filled pad.
+ * tfx_attention_vt: as tfx_attention with V given as that vt; head_dim in
+ * {64, 128}, scale > 0.
+ */
+TFX_API int64_t tfx_attention_vt_ld(int seq);
+TFX_API int tfx_transpose_v(const tfx_half* v, int64_t ld_qkv, tfx_half* vt, int batch, int seq,
+                            int cols, tfx_stream_t stream);
+TFX_API int tfx_attention_vt(const tfx_half* q, const tfx_half* k, const tfx_half* vt,
+                             int64_t ld_qkv, tfx_half* out, int64_t ld_out, int batch, int heads,
+                             int seq, int head_dim, float scale, int causal,
+                             const int32_t* valid_len, tfx_stream_t stream);
+
 /* One pre-norm block's parameters, all device pointers (see tfx_model). */
 typedef struct tfx_layer {
   const float* norm1_weight;  /* [D] */

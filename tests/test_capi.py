@@ -135,3 +135,20 @@ def test_workspace_holds_transposed_v_for_tcgen05_attention(lib):
     expect = up(max(2 * rows * d, vt)) + up(2 * rows * 3 * d) + up(2 * rows * d) + \
         up(4 * rows * d) + up(2 * rows * f)
     assert lib.tfx_forward_workspace_bytes(ctypes.byref(m), b, s) == expect
+
+
+def test_transposed_v_entry_points_validate_on_the_host(lib):
+    pkg = load_package()
+    L = pkg._lib
+    assert lib.tfx_attention_vt_ld(261) == 264
+    assert lib.tfx_attention_vt_ld(0) == -1
+    assert lib.tfx_transpose_v(None, 64, None, 1, 1, 64, None) == L.TFX_ERR_INVALID_ARGUMENT
+    assert lib.tfx_transpose_v(256, 96, 512, 1, 8, 96, None) == L.TFX_ERR_UNSUPPORTED  # cols % 64
+    assert lib.tfx_transpose_v(264, 64, 512, 1, 8, 64, None) == L.TFX_ERR_MISALIGNED
+    # head_dim 32 has no tcgen05 attention kernel
+    assert lib.tfx_attention_vt(256, 512, 768, 96, 1024, 32, 1, 1, 8, 32, 0.17, 1, None,
+                                None) == L.TFX_ERR_UNSUPPORTED
+    assert lib.tfx_attention_vt(256, 512, 768, 192, 1024, 64, 1, 1, 8, 64, -1.0, 1, None,
+                                None) == L.TFX_ERR_UNSUPPORTED
+    assert lib.tfx_attention_vt(None, 512, 768, 192, 1024, 64, 1, 1, 8, 64, 0.125, 1, None,
+                                None) == L.TFX_ERR_INVALID_ARGUMENT

@@ -162,6 +162,48 @@ def test_attention_key_padding(pkg, dev, s, hd):
     assert err < 2e-3, err
 
 
+VT_CASES = [
+    # (batch, seq, heads, hd, causal, lengths or None)
+    (2, 384, 4, 64, True, None),
+    (1, 261, 2, 64, False, None),
+    (3, 300, 2, 128, True, [300, 129, 0]),
+    (4, 200, 4, 64, True, [200, 97, 5, 1]),
+]
+
+
+@pytest.mark.parametrize("b,s,h,hd,causal,lengths", VT_CASES)
+def test_attention_transposed_v_path(pkg, dev, b, s, h, hd, causal, lengths):
+    """The forward's path for head_dim 64/128: tfx_transpose_v (exact, zero
+    padded to a multiple of 8 keys) then tfx_attention_vt."""
+    lib = pkg._lib.load()
+    qkv = _randn(b, s, 3, h, hd, seed=s + hd + b).half()
+    vl = None if lengths is None else torch.tensor(lengths, dtype=torch.int32)
+    ref = _attn_ref(qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2], causal, vl)
+    g = qkv.to(dev)
+    ld_vt = lib.tfx_attention_vt_ld(s)
+    assert ld_vt == (s + 7) // 8 * 8
+    vt = torch.full((b, h * hd, ld_vt), float("nan"), dtype=torch.float16, device=dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    base = g.data_ptr()
+    row = 3 * h * hd
+    pkg._lib.check(lib.tfx_transpose_v(base + 2 * h * hd * 2, row, vt.data_ptr(), b, s, h * hd,
+                                       stream), "tfx_transpose_v")
+    torch.cuda.synchronize()
+    want = g[:, :, 2].reshape(b, s, h * hd).transpose(1, 2)
+    assert torch.equal(vt[:, :, :s], want)
+    assert bool((vt[:, :, s:] == 0).all())
+    out = torch.empty(b, s, h * hd, dtype=torch.float16, device=dev)
+    vl_dev = None if vl is None else vl.to(dev)
+    pkg._lib.check(lib.tfx_attention_vt(base, base + h * hd * 2, vt.data_ptr(), row,
+                                        out.data_ptr(), h * hd, b, h, s, hd, hd ** -0.5,
+                                        int(causal),
+                                        None if vl_dev is None else vl_dev.data_ptr(), stream),
+                   "tfx_attention_vt")
+    torch.cuda.synchronize()
+    err = (out.double().cpu() - ref).abs().max().item()
+    assert err < 2e-3, err
+
+
 def test_attention_long_sequence_rows(pkg, dev):
     """A long causal sequence (S=4096, hd=64): spot-check late query rows
     against the blockwise fp64 oracle."""
