@@ -10,7 +10,7 @@
 //     ctx = attention(qkv)                                    [fp16]
 //     r   = ctx . Wo^T + bo + (l == 0 ? x : r)                [fp32, tcgen05]
 //     h   = LN(r; norm2)                                      [fp16]
-//     g   = gelu_erf(h . W1^T + b1)                           [fp16, tcgen05]
+//     g   = gelu(h . W1^T + b1)  (exact erf form)             [fp16, tcgen05]
 //     r   = g . W2^T + b2 + r                                 [fp32, tcgen05]
 //     h   = LN(r; next norm1)  or  y = LN(r; final_norm)      [fp16 / fp32]
 //

@@ -10,8 +10,12 @@
 // CTA = 6 warps, one CTA per SM, grid = min(#tiles, #SMs):
 //   warp 0      TMA producer (one lane): A and W k-blocks into a STAGES ring
 //   warp 1      TMEM allocator + MMA issuer (one lane)
-//   warps 2..5  epilogue: tcgen05.ld rows out of TMEM, bias / GELU / residual,
-//               store. Warp w may only touch TMEM lanes [32*(w%4), +32).
+//   warps 2..5  epilogue: tcgen05.ld rows out of TMEM, bias / GELU (exact
+//               erf form, Abramowitz & Stegun 7.1.26 erf), then
+//               through a per-warp shared-memory staging tile so that the
+//               residual loads and the output stores are coalesced (a lane
+//               per row would touch 32 rows per warp-wide access). Warp w
+//               may only touch TMEM lanes [32*(w%4), +32).
 #include "internal.h"
 #include "ptx.cuh"
 
@@ -28,7 +32,13 @@ struct GemmLayout {
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kBarOffset = STAGES * kStageBytes;
-  static constexpr int kSmemBytes = kBarOffset + 256 + 1024;  // barriers + 1 KB alignment slack
+  // Epilogue staging: per epilogue warp 32 rows x 32 fp32 columns, rows
+  // padded to 36 floats (16-byte aligned, conflict-free both ways).
+  static constexpr int kStgStride = 36;
+  static constexpr int kStgOffset = kBarOffset + 256;
+  static constexpr int kStgBytes = 4 * 32 * kStgStride * 4;
+  static constexpr int kSmemBytes = kStgOffset + kStgBytes + 1024;  // + 1 KB alignment slack
+  static_assert(kSmemBytes <= 227 * 1024, "shared-memory budget");
   static constexpr uint32_t kTmemCols = (2 * BN) < 32 ? 32 : (2 * BN);
 };
 
@@ -156,51 +166,83 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int m0 = (tile % tiles_m) * kBM;
       const int n0 = (tile / tiles_m) * BN;
-      const int row = m0 + quarter * 32 + lane;
+      const int wrow0 = m0 + quarter * 32;  // this warp's 32 rows
       const uint32_t t_row =
           tmem_base + static_cast<uint32_t>(buf * BN) + (static_cast<uint32_t>(quarter * 32) << 16);
+      float* stg = reinterpret_cast<float*>(smem + L::kStgOffset) + (warp - 2) * 32 * L::kStgStride;
+      // Residual chunks: 8 lanes x float4 = one row's 32 columns, 4 rows per
+      // pass, 8 passes; all 8 loads are issued before the TMEM read so they
+      // are in flight while the accumulator is staged.
+      const int rsub = lane >> 3, rc4 = (lane & 7) * 4;
+      float4 res[8], nxt[8];
+      auto load_res = [&](float4 (&dst)[8], int c) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int row = wrow0 + rsub + 4 * i;
+          dst[i] = row < M ? *reinterpret_cast<const float4*>(residual + row * ldr + n0 + c + rc4)
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      };
+      if constexpr (EPI == TFX_EPI_BIAS_RESIDUAL) load_res(nxt, 0);
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
+        if constexpr (EPI == TFX_EPI_BIAS_RESIDUAL) {
+          // This chunk's residual was loaded one chunk ahead; start the next.
+#pragma unroll
+          for (int i = 0; i < 8; ++i) res[i] = nxt[i];
+          if (c + 32 < BN) load_res(nxt, c + 32);
+        }
         uint32_t r[32];
         tmem_ld32(t_row + c, r);
         tmem_ld_wait();
-        float v[32];
+        // Lane = row: bias (and GELU) in registers, then into the staging tile.
         const float4* b4 = reinterpret_cast<const float4*>(bias + n0 + c);
+        float4* srow = reinterpret_cast<float4*>(stg + lane * L::kStgStride);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const float4 bb = __ldg(b4 + j);
-          v[4 * j + 0] = __uint_as_float(r[4 * j + 0]) + bb.x;
-          v[4 * j + 1] = __uint_as_float(r[4 * j + 1]) + bb.y;
-          v[4 * j + 2] = __uint_as_float(r[4 * j + 2]) + bb.z;
-          v[4 * j + 3] = __uint_as_float(r[4 * j + 3]) + bb.w;
+          float4 v = make_float4(__uint_as_float(r[4 * j + 0]) + bb.x,
+                                 __uint_as_float(r[4 * j + 1]) + bb.y,
+                                 __uint_as_float(r[4 * j + 2]) + bb.z,
+                                 __uint_as_float(r[4 * j + 3]) + bb.w);
+          if constexpr (EPI == TFX_EPI_BIAS_GELU) {
+            v.x = gelu_as(v.x);
+            v.y = gelu_as(v.y);
+            v.z = gelu_as(v.z);
+            v.w = gelu_as(v.w);
+          }
+          srow[j] = v;
         }
-        if (row < M) {
-          if constexpr (EPI == TFX_EPI_BIAS_RESIDUAL) {
-            const float4* res4 = reinterpret_cast<const float4*>(residual + row * ldr + n0 + c);
-            float4* o4 = reinterpret_cast<float4*>(static_cast<float*>(out) + row * ldo + n0 + c);
-            float4 rr[8];
+        __syncwarp();
+        // Row-contiguous phase: consecutive lanes take consecutive columns.
+        if constexpr (EPI == TFX_EPI_BIAS_RESIDUAL) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) rr[j] = res4[j];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              o4[j] = make_float4(v[4 * j] + rr[j].x, v[4 * j + 1] + rr[j].y,
-                                  v[4 * j + 2] + rr[j].z, v[4 * j + 3] + rr[j].w);
+          for (int i = 0; i < 8; ++i) {
+            const int rr = rsub + 4 * i;
+            const int row = wrow0 + rr;
+            if (row < M) {
+              const float4 v = *reinterpret_cast<const float4*>(stg + rr * L::kStgStride + rc4);
+              *reinterpret_cast<float4*>(static_cast<float*>(out) + row * ldo + n0 + c + rc4) =
+                  make_float4(v.x + res[i].x, v.y + res[i].y, v.z + res[i].z, v.w + res[i].w);
             }
-          } else {
-            if constexpr (EPI == TFX_EPI_BIAS_GELU) {
+          }
+        } else {
+          // fp16 out: 4 lanes x 8 halves = one row's 32 columns; 8 rows per pass.
+          const int sub = lane >> 2, c8 = (lane & 3) * 8;
 #pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
-            }
-            uint4* o4 = reinterpret_cast<uint4*>(static_cast<__half*>(out) + row * ldo + n0 + c);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              o4[j] = make_uint4(pack_half2(v[8 * j + 0], v[8 * j + 1]),
-                                 pack_half2(v[8 * j + 2], v[8 * j + 3]),
-                                 pack_half2(v[8 * j + 4], v[8 * j + 5]),
-                                 pack_half2(v[8 * j + 6], v[8 * j + 7]));
+          for (int rr = sub; rr < 32; rr += 8) {
+            const int row = wrow0 + rr;
+            if (row < M) {
+              const float4 v0 = *reinterpret_cast<const float4*>(stg + rr * L::kStgStride + c8);
+              const float4 v1 =
+                  *reinterpret_cast<const float4*>(stg + rr * L::kStgStride + c8 + 4);
+              *reinterpret_cast<uint4*>(static_cast<__half*>(out) + row * ldo + n0 + c + c8) =
+                  make_uint4(pack_half2(v0.x, v0.y), pack_half2(v0.z, v0.w),
+                             pack_half2(v1.x, v1.y), pack_half2(v1.z, v1.w));
             }
           }
         }
+        __syncwarp();  // staging tile reused by the next chunk
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[buf]);

@@ -437,9 +437,5 @@ __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
-__device__ __forceinline__ float gelu_erf(float x) {
-  // Exact GELU, F.gelu(approximate="none"): 0.5 * x * (1 + erf(x / sqrt(2))).
-  return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
-}
 
 }  // namespace tfx
