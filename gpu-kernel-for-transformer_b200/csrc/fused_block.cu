@@ -157,16 +157,24 @@ __device__ __forceinline__ void store_row(uint32_t base, int r, int c0, const fl
   }
 }
 
-__device__ __forceinline__ uint64_t op_desc(uint32_t base, int col) {
-  return sdesc_k_sw128(base + static_cast<uint32_t>((col >> 6) * kBlkBytes + (col & 63) * 2));
+// Descriptor of the K-major operand whose 128-byte-swizzled blocks start at
+// `base`, advanced to column `col`: descriptors are built once per operand
+// region and advanced by adding the column's offset (16-byte units) to the
+// 64-bit value; rebuilding one from an address per MMA puts that arithmetic
+// on the issue path. Shared addresses stay below 2^18, so the 14-bit address
+// field never carries.
+__device__ __forceinline__ uint64_t desc_col(uint64_t base_desc, int col) {
+  return base_desc + static_cast<uint64_t>(((col >> 6) * kBlkBytes + (col & 63) * 2) >> 4);
 }
 
-// D[128 x N] (+)= A[128 x K] . B[N x K]^T over k-steps of 16 starting at K
-// offsets a_col/b_col (both operands K-major in shared memory).
-__device__ __forceinline__ void mma_chain(uint32_t d, uint32_t a, int a_col, uint32_t b,
-                                          int b_col, int ksteps, uint32_t idesc) {
-  for (int k = 0; k < ksteps; ++k)
-    mma_f16_ss(d, op_desc(a, a_col + 16 * k), op_desc(b, b_col + 16 * k), idesc,
+// D[128 x N] (+)= A[128 x K] . B[N x K]^T over KSTEPS k-steps of 16 starting
+// at K offsets a_col/b_col (both operands K-major in shared memory).
+template <int KSTEPS>
+__device__ __forceinline__ void mma_chain(uint32_t d, uint64_t a_desc, int a_col, uint64_t b_desc,
+                                          int b_col, uint32_t idesc) {
+#pragma unroll
+  for (int k = 0; k < KSTEPS; ++k)
+    mma_f16_ss(d, desc_col(a_desc, a_col + 16 * k), desc_col(b_desc, b_col + 16 * k), idesc,
                k > 0 ? 1u : 0u);
 }
 
@@ -413,10 +421,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       return r;
     };
-    auto take_w = [&](uint32_t& w) {
+    const uint64_t dA = sdesc_k_sw128(sA), dK = sdesc_k_sw128(sK), dV = sdesc_k_sw128(sV);
+    const uint64_t dW0 = sdesc_k_sw128(sbase + kOffW);
+    auto take_w = [&](uint64_t& w) {
       if (!mbar_wait(&w_full[slot], ph, p.err, kDevTimeoutFull)) return false;
       tc_fence_after();
-      w = sbase + kOffW + static_cast<uint32_t>(slot * kOpBytes);
+      w = dW0 + static_cast<uint64_t>(slot * (kOpBytes >> 4));
       return true;
     };
     auto release_w = [&]() {
@@ -428,30 +438,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     // D = A . W^T, A the fp16 operand in TMEM A columns.
     auto gemm_tmem_a = [&](uint32_t dcol) {
-      uint32_t w;
+      uint64_t w;
       if (!take_w(w)) return false;
+#pragma unroll
       for (int k = 0; k < kT / 16; ++k)
-        mma_f16_ts(tmem + dcol, tmem + kColA + 8 * k, op_desc(w, 16 * k), id128, k > 0 ? 1u : 0u);
+        mma_f16_ts(tmem + dcol, tmem + kColA + 8 * k, desc_col(w, 16 * k), id128,
+                   k > 0 ? 1u : 0u);
       release_w();
       return true;
     };
     auto issue_s = [&](int h) {  // S_h = Q_h . K_h^T -> S buffer h % 2
-      mma_chain(tmem + ((h & 1) ? kColS1 : kColS0), sA, h * HD, sK, h * HD, HD / 16, id128);
+      mma_chain<HD / 16>(tmem + ((h & 1) ? kColS1 : kColS0), dA, h * HD, dK, h * HD, id128);
       mma_commit(&m2c_s[h & 1]);
     };
     bool ok = true;
     for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
       for (int l = 0; l < L && ok; ++l) {
-        uint32_t w;
+        uint64_t w;
         if (!(ok = wait_c2m())) break;  // LN1 output in sA
         if (!(ok = take_w(w))) break;
-        mma_chain(tmem + 0, sA, 0, w, 0, kT / 16, id128);  // Q
+        mma_chain<kT / 16>(tmem + 0, dA, 0, w, 0, id128);  // Q
         release_w();
         if (!(ok = take_w(w))) break;
-        mma_chain(tmem + 128, sA, 0, w, 0, kT / 16, id128);  // K
+        mma_chain<kT / 16>(tmem + 128, dA, 0, w, 0, id128);  // K
         release_w();
         if (!(ok = take_w(w))) break;
-        mma_chain(tmem + 256, w, 0, sA, 0, kT / 16, id128);  // V^T = Wv . h^T
+        mma_chain<kT / 16>(tmem + 256, w, 0, dA, 0, id128);  // V^T = Wv . h^T
         release_w();
         mma_commit(m2c_g);
         if (!(ok = wait_c2m())) break;  // Q, K, V^T in smem
@@ -465,10 +477,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t sb = (h & 1) ? kColS1 : kColS0;
           // P_h: keys [0,64) in columns [0,32) of its S buffer, keys [64,128)
           // in columns [64,96) (each compute warp packs over its own S half).
+          const uint64_t dVh = dV + static_cast<uint64_t>((h * HD * 128) >> 4);
+#pragma unroll
           for (int k = 0; k < kT / 16; ++k)
             mma_f16_ts(tmem + kColO + (h & 1) * HD, tmem + sb + (k < 4 ? 8 * k : 64 + 8 * (k - 4)),
-                       op_desc(sV + static_cast<uint32_t>(h * HD * 128), 16 * k), idhd,
-                       k > 0 ? 1u : 0u);
+                       desc_col(dVh, 16 * k), idhd, k > 0 ? 1u : 0u);
           mma_commit(&m2c_o[h & 1]);
           if (h + 2 < H) {
             // S_{h+2} reuses the columns P_h is read from: wait until P_h.V_h
@@ -481,7 +494,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!ok || !(ok = wait_c2m())) break;  // ctx complete in sA
         if (!(ok = take_w(w))) break;
-        mma_chain(tmem + 0, sA, 0, w, 0, kT / 16, id128);  // out-proj
+        mma_chain<kT / 16>(tmem + 0, dA, 0, w, 0, id128);  // out-proj
         release_w();
         mma_commit(m2c_g);
         if (!(ok = wait_c2m())) break;  // LN2 output in TMEM A
@@ -663,8 +676,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_ld_row(sb + 64 * half + 32 * c, sc);
             const int k0 = 32 * (2 * half + c);
             if (plain[c]) {
+              float m8[8];
 #pragma unroll
-              for (int j = 0; j < 32; ++j) mx = fmaxf(mx, sc[j]);
+              for (int i = 0; i < 8; ++i) m8[i] = fmax3(sc[i], sc[i + 8], sc[i + 16]);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) m8[i] = fmax3(m8[i], sc[i + 24], mx);
+              mx = fmaxf(fmax3(m8[0], m8[1], m8[2]), fmax3(fmax3(m8[3], m8[4], m8[5]), m8[6], m8[7]));
             } else {
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
@@ -676,8 +693,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           mx = fmaxf(mx, pr.swap(make_float2(mx, 0.f)).x);
           // All keys padding (zero-length sequence): weights exp2(-inf) = 0.
           const float mref = (mx == -INFINITY) ? 0.f : mx * sl2;
-          // Pass 2: exp2, row sum, fp16 packing.
+          // Pass 2: exp2, row sum, fp16 packing (f32x2 pairs on plain chunks;
+          // 2 of every 8 pairs through the FMA-pipe polynomial).
           float sum2[2] = {0.f, 0.f};
+          uint64_t ls0 = 0, ls1 = 0;
+          const uint64_t c2 = f2_pack(sl2, sl2), negm2 = f2_pack(-mref, -mref);
           uint32_t w[32];
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
@@ -685,21 +705,43 @@ __global__ void __launch_bounds__(kThreads, 1)
               float sc[32];
               tmem_ld_row(sb + 64 * half + 32 * c, sc);
               const int k0 = 32 * (2 * half + c);
+              if (plain[c]) {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                float ex = fast_exp2(fmaf(sc[j], sl2, -mref));
-                if (!plain[c] && (k0 + j < kl_e || k0 + j > kh_e)) ex = 0.f;
-                sc[j] = ex;
-                sum2[j & 1] += ex;
+                for (int j = 0; j < 16; ++j) {
+                  const uint64_t arg = f2_fma(f2_pack(sc[2 * j], sc[2 * j + 1]), c2, negm2);
+                  uint64_t e;
+                  if ((j & 7) < 2) {
+                    e = exp2_poly_f2(arg);
+                  } else {
+                    float a0, a1;
+                    f2_unpack(arg, a0, a1);
+                    e = f2_pack(fast_exp2(a0), fast_exp2(a1));
+                  }
+                  if (j & 1) ls1 = f2_add(ls1, e); else ls0 = f2_add(ls0, e);
+                  float e0, e1;
+                  f2_unpack(e, e0, e1);
+                  w[16 * c + j] = pack_half2(e0, e1);
+                }
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                  float ex = fast_exp2(fmaf(sc[j], sl2, -mref));
+                  if (k0 + j < kl_e || k0 + j > kh_e) ex = 0.f;
+                  sc[j] = ex;
+                  sum2[j & 1] += ex;
+                }
+#pragma unroll
+                for (int j = 0; j < 16; ++j) w[16 * c + j] = pack_half2(sc[2 * j], sc[2 * j + 1]);
               }
-#pragma unroll
-              for (int j = 0; j < 16; ++j) w[16 * c + j] = pack_half2(sc[2 * j], sc[2 * j + 1]);
             } else {
 #pragma unroll
               for (int j = 0; j < 16; ++j) w[16 * c + j] = 0u;
             }
           }
-          const float sum = sum2[0] + sum2[1];
+          float la, lb, lc, ld;
+          f2_unpack(ls0, la, lb);
+          f2_unpack(ls1, lc, ld);
+          const float sum = (sum2[0] + sum2[1]) + ((la + lb) + (lc + ld));
           psum[(b * 2 + half) * kT + r] = sum;
           tmem_st32(sb + 64 * half, w);  // P over this warp's own S columns
           tmem_st_wait();
