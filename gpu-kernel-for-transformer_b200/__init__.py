@@ -12,6 +12,7 @@ The directory name is not a Python identifier; import it with
 
 from . import _lib, ops, sharding  # noqa: F401
 from .graph import FixedInputCUDAGraph, ForwardGraph, maybe_cuda_graph  # noqa: F401
+from .streaming import StreamingForward  # noqa: F401
 from .model import (  # noqa: F401
     OFFICIAL_BENCHMARK_SHAPES,
     BaselineTransformer,
@@ -29,6 +30,7 @@ __all__ = [
     "FixedInputCUDAGraph",
     "ForwardGraph",
     "maybe_cuda_graph",
+    "StreamingForward",
     "ops",
     "sharding",
 ]

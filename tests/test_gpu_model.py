@@ -187,3 +187,25 @@ def test_fused_forward_and_op_chain_match_oracle(pkg, dev, case):
 def test_no_device_timeout_after_fused(pkg, dev):
     torch.cuda.synchronize()
     assert pkg._lib.read_device_error() == 0
+
+
+@pytest.mark.parametrize("cfg", [
+    dict(batch_size=4, seq_len=128, d_model=128, num_heads=4, ffn_dim=128, num_layers=2,
+         causal=True),   # fused whole-forward kernel
+    dict(batch_size=2, seq_len=96, d_model=256, num_heads=4, ffn_dim=256, num_layers=2,
+         causal=True),   # per-op chain (workspace shared across steps)
+])
+def test_streaming_forward_matches_model(pkg, dev, cfg):
+    """Pipelined host-to-host forward of 5 different batches (slots reused)
+    equals model(x) batch by batch, bit for bit."""
+    _, cand = _pair(pkg, cfg, 1234, dev)
+    b, s, d = cfg["batch_size"], cfg["seq_len"], cfg["d_model"]
+    xs = [torch.randn(b, s, d, generator=torch.Generator().manual_seed(40 + i)).pin_memory()
+          for i in range(5)]
+    ys = [torch.full((b, s, d), float("nan")).pin_memory() for _ in range(5)]
+    sf = pkg.StreamingForward(cand, dev, b, s)
+    with torch.inference_mode():
+        done = sf.run(xs, ys)
+        done.synchronize()
+        for x, y in zip(xs, ys):
+            assert torch.equal(y, cand(x.to(dev)).cpu())
