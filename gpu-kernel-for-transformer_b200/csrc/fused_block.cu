@@ -667,13 +667,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             in[c] = ch >= lo_e && ch <= hi_e;  // warp-uniform
             plain[c] = plain_tile && (!p.causal || ch < qq_e);
           }
-          // Pass 1: masked row max (one chunk live at a time).
+          // Pass 1: masked row max. Both chunks come in with one TMEM round
+          // trip (pass 2 reloads them one at a time: keeping both live across
+          // the exchange would spill).
           float mx = -INFINITY;
+          uint32_t sr[2][32];
+          tmem_ld32(sb + 64 * half, sr[0]);
+          tmem_ld32(sb + 64 * half + 32, sr[1]);
+          tmem_ld_wait();
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             if (!in[c]) continue;
             float sc[32];
-            tmem_ld_row(sb + 64 * half + 32 * c, sc);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) sc[j] = __uint_as_float(sr[c][j]);
             const int k0 = 32 * (2 * half + c);
             if (plain[c]) {
               float m8[8];
@@ -769,10 +776,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!(ok = wait(m2c_g, ph_g))) break;  // FFN-in accumulator
         {
           float v[2][32];
+          {
+            uint32_t g0[32], g1[32];  // both chunks, one TMEM round trip
+            tmem_ld32(tl + kColF + 64 * half, g0);
+            tmem_ld32(tl + kColF + 64 * half + 32, g1);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              v[0][j] = __uint_as_float(g0[j]);
+              v[1][j] = __uint_as_float(g1[j]);
+            }
+          }
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             const int col = 64 * half + 32 * c;
-            tmem_ld_row(tl + kColF + col, v[c]);
             add_bias32(v[c], lp + kPIn + col);
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[c][j] = gelu_as(v[c][j]);
