@@ -706,11 +706,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint64_t ls0 = 0, ls1 = 0;
           const uint64_t c2 = f2_pack(sl2, sl2), negm2 = f2_pack(-mref, -mref);
           uint32_t w[32];
+          uint32_t sr2[2][32];  // both chunks, one TMEM round trip
+          tmem_ld32(sb + 64 * half, sr2[0]);
+          tmem_ld32(sb + 64 * half + 32, sr2[1]);
+          tmem_ld_wait();
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             if (in[c]) {
               float sc[32];
-              tmem_ld_row(sb + 64 * half + 32 * c, sc);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) sc[j] = __uint_as_float(sr2[c][j]);
               const int k0 = 32 * (2 * half + c);
               if (plain[c]) {
 #pragma unroll
