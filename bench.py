@@ -275,7 +275,9 @@ def run_reference(args):
 
 def kernel_breakdown(pkg, model, x, ws, steps):
     """Re-issue the per-op chain's launch sequence kernel by kernel through
-    the C ABI with CUDA events between launches; {kind: [ms per launch]}."""
+    the C ABI with CUDA events between launches; {kind: [ms per launch]}.
+    Each step's launches are queued behind a short device-side sleep, so
+    they run back to back on the GPU as in the forward itself."""
     import torch
 
     lib = pkg._lib.load()
@@ -313,6 +315,10 @@ def kernel_breakdown(pkg, model, x, ws, steps):
         times.setdefault(kind, []).append((e0, e1))
 
     for _ in range(steps):
+        # Hold the stream for ~2 ms so the host enqueues this step's launches
+        # (and their events) ahead of the GPU: the events then bracket GPU
+        # execution only, not the host's launch latency between calls.
+        torch.cuda._sleep(4_000_000)
         timed("layernorm", lambda: lib.tfx_layer_norm(
             x.data_ptr(), layers[0].norm1_weight, layers[0].norm1_bias, h, 0, M, D, eps, 1,
             stream))
