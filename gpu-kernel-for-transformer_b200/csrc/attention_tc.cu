@@ -66,21 +66,25 @@ constexpr uint32_t kTmemCols = 512;
 
 template <int HD>
 struct TcAttn {
-  static constexpr int kStages = HD == 64 ? 4 : 2;
+  // Query tiles per CTA: two share each K/V tile; head_dim 256 has room
+  // (TMEM: S 128 + P 64 + O 256 columns; shared memory: Q, K, V 64 KB each)
+  // for one.
+  static constexpr int kNT = HD == 256 ? 1 : 2;
+  static constexpr int kStages = HD == 64 ? 4 : (HD == 128 ? 2 : 1);
   static constexpr int kBlocks = HD / 64;            // 128-byte column blocks per row
   static constexpr int kBlockBytes = kTile * 128;    // one 64-column block of a tile
   static constexpr int kTileBytes = kTile * HD * 2;  // one Q/K/V tile, fp16
   static constexpr int kVtBoxBytes = HD * 128;        // V^T box: HD rows x 64 keys
-  static constexpr int kQ = 0;                        // Q_A, Q_B
-  static constexpr int kK = 2 * kTileBytes;
+  static constexpr int kQ = 0;                        // Q_A (, Q_B)
+  static constexpr int kK = kNT * kTileBytes;
   static constexpr int kV = kK + kStages * kTileBytes;
   static constexpr int kBar = kV + kStages * kTileBytes;
-  static constexpr int kSmem = kBar + 256 + 1024;    // barriers + alignment slack
-  static constexpr bool kSepP = HD == 64;                 // P has its own TMEM columns
-  static constexpr uint32_t kColP = kSepP ? 2 * kTile : 0;
+  static constexpr int kSmem = kBar + 512 + 1024;    // barriers + alignment slack
+  static constexpr bool kSepP = HD != 128;                // P has its own TMEM columns
+  static constexpr uint32_t kColP = kSepP ? kNT * kTile : 0;
   static constexpr uint32_t kPStride = kSepP ? kTile / 2 : kTile;
-  static constexpr uint32_t kColO = kSepP ? 3 * kTile : 2 * kTile;
-  static_assert(kColO + 2 * HD <= kTmemCols, "TMEM budget");
+  static constexpr uint32_t kColO = kNT == 1 ? 2 * kTile : (kSepP ? 3 * kTile : 2 * kTile);
+  static_assert(kColO + kNT * HD <= kTmemCols, "TMEM budget");
   static_assert(kSmem <= 227 * 1024, "shared-memory budget");
 };
 
@@ -99,8 +103,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* q_full = reinterpret_cast<uint64_t*>(smem + L::kBar);
   uint64_t* k_full = q_full + 1;
   uint64_t* v_full = k_full + S;
-  uint64_t* kv_empty = v_full + S;  // [2][S]: stage free for tile X (its MMAs completed)
-  uint64_t* s_full = kv_empty + 2 * S;  // [2]: S_X computed
+  // K and V stages are released separately (K after its QK^T, V after its
+  // P.V), per query tile: with one stage the next K must load before P.V.
+  uint64_t* k_empty = v_full + S;       // [2][S]
+  uint64_t* v_empty = k_empty + 2 * S;  // [2][S]
+  uint64_t* s_full = v_empty + 2 * S;   // [2]: S_X computed
   uint64_t* s_free = s_full + 2;    // [2]: S_X read into registers (separate P only), 4 warps
   uint64_t* p_full = s_free + 2;    // [2]: P_X written (and O_X rescaled), 4 warps arrive
   uint64_t* o_done = p_full + 2;    // [2]: O_X += P_X V completed
@@ -113,7 +120,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int b = static_cast<int>(blockIdx.x / heads);
   // Causal: the heaviest query blocks (the last ones) are launched first.
   const int qb = CAUSAL ? nqb - 1 - static_cast<int>(blockIdx.y) : static_cast<int>(blockIdx.y);
-  const int q0 = qb * 2 * kTile;
+  const int q0 = qb * L::kNT * kTile;
   const int kend = valid_len ? min(seq, max(0, valid_len[b])) : seq;
   auto tiles_for = [&](int qx) {
     if (qx >= seq) return 0;
@@ -121,7 +128,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     return (lim + kTile - 1) / kTile;
   };
   const int nA = tiles_for(q0);
-  const int nB = tiles_for(q0 + kTile);
+  const int nB = L::kNT == 2 ? tiles_for(q0 + kTile) : 0;
   const int n_iter = max(nA, nB);
 
   if (threadIdx.x == 0) {
@@ -132,8 +139,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     for (int s = 0; s < S; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
-      mbar_init(&kv_empty[S + s], 1);
+      for (int x = 0; x < 2; ++x) {
+        mbar_init(&k_empty[x * S + s], 1);
+        mbar_init(&v_empty[x * S + s], 1);
+      }
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(&s_full[x], 1);
@@ -158,26 +167,32 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // ------------------------------------------------------ TMA producer
     if (lane == 0) {
       const int col0 = h * HD;
-      mbar_arrive_expect_tx(q_full, 2 * L::kTileBytes);
+      mbar_arrive_expect_tx(q_full, L::kNT * L::kTileBytes);
 #pragma unroll
-      for (int x = 0; x < 2; ++x)
+      for (int x = 0; x < L::kNT; ++x)
 #pragma unroll
         for (int cb = 0; cb < L::kBlocks; ++cb)
           tma_load_3d(smem + L::kQ + x * L::kTileBytes + cb * L::kBlockBytes, &tm_q, q_full,
                       col0 + 64 * cb, q0 + x * kTile, b);
-      int issued = 0;
+      int issued = 0, k_issued = 0;
       for (int j = 0; j < n_iter; ++j) {
         const int st = j % S;
-        if (j >= S) {  // stage st last held tile j - S: wait for the tiles that used it
-          const uint32_t par = ((j / S) - 1) & 1;
-          if (j - S < nA && !mbar_wait(&kv_empty[st], par, err, kDevTimeoutEmpty)) break;
-          if (j - S < nB && !mbar_wait(&kv_empty[S + st], par, err, kDevTimeoutEmpty)) break;
+        // Stage st last held tile j - S: wait for the query tiles that used it.
+        const uint32_t par = ((j / S) - 1) & 1;
+        if (j >= S) {
+          if (j - S < nA && !mbar_wait(&k_empty[st], par, err, kDevTimeoutEmpty)) break;
+          if (j - S < nB && !mbar_wait(&k_empty[S + st], par, err, kDevTimeoutEmpty)) break;
         }
         mbar_arrive_expect_tx(&k_full[st], L::kTileBytes);
 #pragma unroll
         for (int cb = 0; cb < L::kBlocks; ++cb)
           tma_load_3d(smem + L::kK + st * L::kTileBytes + cb * L::kBlockBytes, &tm_k, &k_full[st],
                       col0 + 64 * cb, j * kTile, b);
+        k_issued = j + 1;
+        if (j >= S) {
+          if (j - S < nA && !mbar_wait(&v_empty[st], par, err, kDevTimeoutEmpty)) break;
+          if (j - S < nB && !mbar_wait(&v_empty[S + st], par, err, kDevTimeoutEmpty)) break;
+        }
         mbar_arrive_expect_tx(&v_full[st], L::kTileBytes);
         if constexpr (VT) {  // V^T rows h*HD.. (+HD), keys j*128.. in two 64-key boxes
 #pragma unroll
@@ -195,17 +210,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       // Our own copies land before the CTA may exit (after a timeout nobody
       // else waits for them); on the normal path these phases are complete.
       mbar_wait(q_full, 0, nullptr, 0);
-      for (int j = max(0, issued - S); j < issued; ++j) {
+      for (int j = max(0, k_issued - S); j < k_issued; ++j)
         mbar_wait(&k_full[j % S], (j / S) & 1, nullptr, 0);
+      for (int j = max(0, issued - S); j < issued; ++j)
         mbar_wait(&v_full[j % S], (j / S) & 1, nullptr, 0);
-      }
     }
   } else if (warp == 1 || warp == 10) {
     // ------------------------------------------------ MMA issuer of tile x
     if (lane == 0) {
       const int x = warp == 1 ? 0 : 1;
       const int nx = x == 0 ? nA : nB;
-      uint64_t* kv_free = kv_empty + x * S;
+      uint64_t* k_free = k_empty + x * S;
+      uint64_t* v_free = v_empty + x * S;
       constexpr uint32_t id_qk = idesc_f16_f32(kTile, kTile);
       constexpr uint32_t id_pv = VT ? idesc_f16_f32(kTile, HD) : idesc_f16_f32_bmn(kTile, HD);
       // Descriptors are built once; each MMA adds a constant to the 64-bit
@@ -246,6 +262,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           tc_fence_after();
           issue_qk(x, 0);
           mma_commit(&s_full[x]);
+          mma_commit(&k_free[0]);
         }
       }
       for (int j = 0; ok && j < nx; ++j) {
@@ -261,20 +278,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             tc_fence_after();
             issue_qk(x, st1);
             mma_commit(&s_full[x]);
+            mma_commit(&k_free[st1]);  // K_{j+1} is free for this tile
           }
           if (!mbar_wait(&v_full[st], par, err, kDevTimeoutFull)) break;
           if (!mbar_wait(&p_full[x], jp, err, kDevTimeoutOther)) break;
           tc_fence_after();
           issue_pv(x, st, j > 0);
           mma_commit(&o_done[x]);
-          mma_commit(&kv_free[st]);  // K_j and V_j are free for this tile
+          mma_commit(&v_free[st]);  // V_j is free for this tile
         } else {
           if (!mbar_wait(&v_full[st], par, err, kDevTimeoutFull)) break;
           if (!mbar_wait(&p_full[x], jp, err, kDevTimeoutOther)) break;
           tc_fence_after();
           issue_pv(x, st, j > 0);
           mma_commit(&o_done[x]);
-          mma_commit(&kv_free[st]);
+          mma_commit(&v_free[st]);
           if (j + 1 < nx) {
             // S_X(j+1) overwrites P_X(j): wait for PV_X(j) to finish reading it.
             if (!mbar_wait(&k_full[st1], par1, err, kDevTimeoutFull)) break;
@@ -282,6 +300,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             tc_fence_after();
             issue_qk(x, st1);
             mma_commit(&s_full[x]);
+            mma_commit(&k_free[st1]);
           }
         }
       }
@@ -292,6 +311,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   } else {
     // ------------------------------------------------------------ softmax
     const int x = (warp - 2) >> 2;  // 0: tile A, 1: tile B
+    if (x < L::kNT) {
     const int quarter = warp & 3;   // this warp's TMEM lanes [32*quarter, +32)
     const int row = quarter * 32 + lane;
     const int qx = q0 + x * kTile;
@@ -436,6 +456,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
       for (int i = 0; i < HD / 8; ++i) d4[i] = make_uint4(0, 0, 0, 0);
     }
+    }  // x < kNT
   }
 
   tc_fence_before();
@@ -500,7 +521,7 @@ int launch_tc(const __half* q, const __half* k, const __half* v, int64_t ld_qkv,
                         static_cast<uint64_t>(ld_qkv), bstride, 64, kTile);
   }
   if (st != TFX_OK) return st;
-  const int nqb = (seq + 2 * kTile - 1) / (2 * kTile);
+  const int nqb = (seq + L::kNT * kTile - 1) / (L::kNT * kTile);
   const dim3 grid(static_cast<unsigned>(batch) * static_cast<unsigned>(heads),
                   static_cast<unsigned>(nqb));
   kern<<<grid, kTcThreads, L::kSmem, stream>>>(tq, tk, tv, out, ld_out, heads, seq, nqb,
@@ -513,8 +534,7 @@ template <bool VT>
 int dispatch_tc(const __half* q, const __half* k, const __half* v, int64_t ld_qkv, int64_t ld_vt,
                 __half* out, int64_t ld_out, int batch, int heads, int seq, int head_dim,
                 float scale, int causal, const int32_t* valid_len, cudaStream_t stream) {
-  if (static_cast<int64_t>(batch) * heads > 0x7fffffff ||
-      (seq + 2 * kTile - 1) / (2 * kTile) > 65535)
+  if (static_cast<int64_t>(batch) * heads > 0x7fffffff || (seq + kTile - 1) / kTile > 65535)
     return fail(TFX_ERR_UNSUPPORTED, "tfx_attention: batch*heads or seq too large for the grid");
   if (head_dim == 64)
     return causal ? launch_tc<64, true, VT>(q, k, v, ld_qkv, ld_vt, out, ld_out, batch, heads,
@@ -526,13 +546,18 @@ int dispatch_tc(const __half* q, const __half* k, const __half* v, int64_t ld_qk
                                              seq, scale, valid_len, stream)
                   : launch_tc<128, false, VT>(q, k, v, ld_qkv, ld_vt, out, ld_out, batch, heads,
                                               seq, scale, valid_len, stream);
-  return fail(TFX_ERR_UNSUPPORTED, "attention_tc: head_dim %d not in {64,128}", head_dim);
+  if (head_dim == 256)
+    return causal ? launch_tc<256, true, VT>(q, k, v, ld_qkv, ld_vt, out, ld_out, batch, heads,
+                                             seq, scale, valid_len, stream)
+                  : launch_tc<256, false, VT>(q, k, v, ld_qkv, ld_vt, out, ld_out, batch, heads,
+                                              seq, scale, valid_len, stream);
+  return fail(TFX_ERR_UNSUPPORTED, "attention_tc: head_dim %d not in {64,128,256}", head_dim);
 }
 
 }  // namespace
 
 bool attention_tc_supported(int head_dim, float scale) {
-  return (head_dim == 64 || head_dim == 128) && scale > 0.f;
+  return (head_dim == 64 || head_dim == 128 || head_dim == 256) && scale > 0.f;
 }
 
 int launch_attention_tc(const __half* q, const __half* k, const __half* v, int64_t ld_qkv,

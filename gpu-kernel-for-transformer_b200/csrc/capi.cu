@@ -275,7 +275,7 @@ int tfx_attention_vt(const tfx_half* q, const tfx_half* k, const tfx_half* vt, i
   if (batch <= 0 || heads <= 0 || seq <= 0 || head_dim <= 0)
     return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_attention_vt: sizes must be positive");
   if (!attention_tc_supported(head_dim, scale))
-    return fail(TFX_ERR_UNSUPPORTED, "tfx_attention_vt: head_dim %d not in {64,128} or scale <= 0",
+    return fail(TFX_ERR_UNSUPPORTED, "tfx_attention_vt: head_dim %d not in {64,128,256} or scale <= 0",
                 head_dim);
   if (heads > 65535 || batch > 65535)
     return fail(TFX_ERR_UNSUPPORTED, "tfx_attention_vt: batch and heads must be <= 65535");

@@ -53,7 +53,9 @@ struct Workspace {
 
 // The tcgen05 attention path (head_dim 64/128) reads V transposed; the copy
 // lives in h's buffer, which is dead between the QKV GEMM and LayerNorm 2.
-bool attention_reads_vt(int hd) { return attention_tc_supported(hd, 1.0f); }
+// (head_dim 256 keeps V in place: one K/V tile per query tile at the lengths
+// it is used with, where the transpose would cost more than it saves.)
+bool attention_reads_vt(int hd) { return hd == 64 || hd == 128; }
 
 Workspace plan_workspace(char* base, int batch, int seq, int d, int f, int hd) {
   Workspace w{};

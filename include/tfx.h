@@ -128,7 +128,7 @@ TFX_API int tfx_attention(const tfx_half* q, const tfx_half* k, const tfx_half* 
  * (cols = H*head_dim, a multiple of 64), s < seq; row pitch
  * tfx_attention_vt_ld(seq) elements (seq rounded up to 8), zero-filled pad.
  * tfx_attention_vt: as tfx_attention with V given as that vt; head_dim in
- * {64, 128}, scale > 0.
+ * {64, 128, 256}, scale > 0.
  */
 TFX_API int64_t tfx_attention_vt_ld(int seq);
 TFX_API int tfx_transpose_v(const tfx_half* v, int64_t ld_qkv, tfx_half* vt, int batch, int seq,

@@ -168,6 +168,10 @@ VT_CASES = [
     (1, 261, 2, 64, False, None),
     (3, 300, 2, 128, True, [300, 129, 0]),
     (4, 200, 4, 64, True, [200, 97, 5, 1]),
+    # head_dim 256: one query tile per CTA, one K/V stage
+    (2, 128, 4, 256, True, None),
+    (1, 300, 2, 256, True, [300]),
+    (2, 136, 2, 256, False, [136, 57]),
 ]
 
 
