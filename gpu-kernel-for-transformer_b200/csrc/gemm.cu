@@ -184,6 +184,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       };
       if constexpr (EPI == TFX_EPI_BIAS_RESIDUAL) load_res(nxt, 0);
+      // The next chunk's TMEM load is in flight while this chunk is stored.
+      uint32_t r[32];
+      tmem_ld32(t_row, r);
+      const int sub = lane >> 2, c8 = (lane & 3) * 8;  // fp16 out: 4 lanes per row, 8 rows/pass
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         if constexpr (EPI == TFX_EPI_BIAS_RESIDUAL) {
@@ -192,30 +196,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 8; ++i) res[i] = nxt[i];
           if (c + 32 < BN) load_res(nxt, c + 32);
         }
-        uint32_t r[32];
-        tmem_ld32(t_row + c, r);
         tmem_ld_wait();
-        // Lane = row: bias (and GELU) in registers, then into the staging tile.
-        const float4* b4 = reinterpret_cast<const float4*>(bias + n0 + c);
+        // Lane = row: the raw accumulator into the staging tile.
         float4* srow = reinterpret_cast<float4*>(stg + lane * L::kStgStride);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float4 bb = __ldg(b4 + j);
-          float4 v = make_float4(__uint_as_float(r[4 * j + 0]) + bb.x,
-                                 __uint_as_float(r[4 * j + 1]) + bb.y,
-                                 __uint_as_float(r[4 * j + 2]) + bb.z,
-                                 __uint_as_float(r[4 * j + 3]) + bb.w);
-          if constexpr (EPI == TFX_EPI_BIAS_GELU) {
-            v.x = gelu_as(v.x);
-            v.y = gelu_as(v.y);
-            v.z = gelu_as(v.z);
-            v.w = gelu_as(v.w);
-          }
-          srow[j] = v;
-        }
+        for (int j = 0; j < 8; ++j)
+          srow[j] = make_float4(__uint_as_float(r[4 * j + 0]), __uint_as_float(r[4 * j + 1]),
+                                __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
         __syncwarp();
-        // Row-contiguous phase: consecutive lanes take consecutive columns.
+        if (c + 32 < BN) tmem_ld32(t_row + c + 32, r);
+        // Row-contiguous phase: consecutive lanes take consecutive columns, so
+        // each lane needs only its own columns' bias.
         if constexpr (EPI == TFX_EPI_BIAS_RESIDUAL) {
+          const float4 bb = __ldg(reinterpret_cast<const float4*>(bias + n0 + c + rc4));
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const int rr = rsub + 4 * i;
@@ -223,12 +216,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (row < M) {
               const float4 v = *reinterpret_cast<const float4*>(stg + rr * L::kStgStride + rc4);
               *reinterpret_cast<float4*>(static_cast<float*>(out) + row * ldo + n0 + c + rc4) =
-                  make_float4(v.x + res[i].x, v.y + res[i].y, v.z + res[i].z, v.w + res[i].w);
+                  make_float4((v.x + bb.x) + res[i].x, (v.y + bb.y) + res[i].y,
+                              (v.z + bb.z) + res[i].z, (v.w + bb.w) + res[i].w);
             }
           }
         } else {
-          // fp16 out: 4 lanes x 8 halves = one row's 32 columns; 8 rows per pass.
-          const int sub = lane >> 2, c8 = (lane & 3) * 8;
+          const float4 b0 = __ldg(reinterpret_cast<const float4*>(bias + n0 + c + c8));
+          const float4 b1 = __ldg(reinterpret_cast<const float4*>(bias + n0 + c + c8 + 4));
 #pragma unroll
           for (int rr = sub; rr < 32; rr += 8) {
             const int row = wrow0 + rr;
@@ -236,9 +230,15 @@ __global__ void __launch_bounds__(kThreads, 1)
               const float4 v0 = *reinterpret_cast<const float4*>(stg + rr * L::kStgStride + c8);
               const float4 v1 =
                   *reinterpret_cast<const float4*>(stg + rr * L::kStgStride + c8 + 4);
+              float e[8] = {v0.x + b0.x, v0.y + b0.y, v0.z + b0.z, v0.w + b0.w,
+                            v1.x + b1.x, v1.y + b1.y, v1.z + b1.z, v1.w + b1.w};
+              if constexpr (EPI == TFX_EPI_BIAS_GELU) {
+#pragma unroll
+                for (int u = 0; u < 8; ++u) e[u] = gelu_as(e[u]);
+              }
               *reinterpret_cast<uint4*>(static_cast<__half*>(out) + row * ldo + n0 + c + c8) =
-                  make_uint4(pack_half2(v0.x, v0.y), pack_half2(v0.z, v0.w),
-                             pack_half2(v1.x, v1.y), pack_half2(v1.z, v1.w));
+                  make_uint4(pack_half2(e[0], e[1]), pack_half2(e[2], e[3]),
+                             pack_half2(e[4], e[5]), pack_half2(e[6], e[7]));
             }
           }
         }
