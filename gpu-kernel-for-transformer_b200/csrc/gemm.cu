@@ -39,7 +39,9 @@ struct GemmLayout {
   static constexpr int kStgBytes = 4 * 32 * kStgStride * 4;
   static constexpr int kSmemBytes = kStgOffset + kStgBytes + 1024;  // + 1 KB alignment slack
   static_assert(kSmemBytes <= 227 * 1024, "shared-memory budget");
-  static constexpr uint32_t kTmemCols = (2 * BN) < 32 ? 32 : (2 * BN);
+  // Two accumulator buffers; TMEM allocations are powers of two >= 32 columns.
+  static constexpr uint32_t kTmemCols = 2 * BN <= 32 ? 32 : 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128
+                                      : 2 * BN <= 256 ? 256 : 512;
 };
 
 template <int BN, int STAGES, int EPI>
@@ -179,7 +181,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const int row = wrow0 + rsub + 4 * i;
-          dst[i] = row < M ? *reinterpret_cast<const float4*>(residual + row * ldr + n0 + c + rc4)
+          // Read exactly once: evict-first, so the reused A/W tiles stay in L2.
+          dst[i] = row < M ? __ldcs(reinterpret_cast<const float4*>(residual + row * ldr + n0 + c + rc4))
                            : make_float4(0.f, 0.f, 0.f, 0.f);
         }
       };
@@ -285,9 +288,23 @@ template <int EPI>
 int launch_gemm_epi(const __half* a, int64_t lda, const __half* w, const float* bias,
                     const float* residual, int64_t ldr, void* out, int64_t ldo, int64_t m, int n,
                     int k, cudaStream_t stream) {
-  // Widest N tile that divides n: fewer, larger MMAs and fewer A re-reads.
-  if (n % 256 == 0 && n > 128)
+  // N tile: wide tiles mean fewer A re-reads, but the tile count should also
+  // fill the last wave of the persistent grid (768 tiles of 256 on 148 SMs
+  // are 5.19 waves; 1024 tiles of 192 are 6.92). Score = wave efficiency,
+  // discounted for the narrower tile's extra operand traffic.
+  const int sms = num_sms();
+  const int64_t mt = (m + kBM - 1) / kBM;
+  auto score = [&](int bn, double per_tile) {
+    if (n % bn != 0) return 0.0;
+    const int64_t t = mt * (n / bn);
+    const int64_t waves = (t + sms - 1) / sms;
+    return per_tile * static_cast<double>(t) / static_cast<double>(waves * sms);
+  };
+  const double s256 = score(256, 1.0), s192 = score(192, 0.97), s128 = score(128, 0.92);
+  if (s256 > 0 && s256 >= s192 && s256 >= s128)
     return launch_gemm_t<256, 4, EPI>(a, lda, w, bias, residual, ldr, out, ldo, m, n, k, stream);
+  if (s192 > 0 && s192 >= s128)
+    return launch_gemm_t<192, 5, EPI>(a, lda, w, bias, residual, ldr, out, ldo, m, n, k, stream);
   if (n % 128 == 0)
     return launch_gemm_t<128, 6, EPI>(a, lda, w, bias, residual, ldr, out, ldo, m, n, k, stream);
   if (n % 64 == 0)
