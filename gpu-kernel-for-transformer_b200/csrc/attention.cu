@@ -78,6 +78,8 @@ __global__ void __launch_bounds__(kAttnThreads)
                          const __half* __restrict__ v, int64_t ld_qkv, __half* __restrict__ out,
                          int64_t ld_out, int heads, int seq, float scale_log2,
                          const int32_t* __restrict__ valid_len) {
+  grid_dep_wait();
+  grid_dep_launch();
   using C = AttnCfg<HD>;
   constexpr int HDP = C::kHDP, BKV = C::kBKV;
   constexpr int NT_S = BKV / 8;  // score n-tiles per warp
@@ -274,14 +276,14 @@ int launch_hd(const __half* q, const __half* k, const __half* v, int64_t ld_qkv,
     auto kern = attention_mma_kernel<HD, true>;
     int st = ensure_smem(reinterpret_cast<const void*>(kern), C::kSmemBytes, done_c);
     if (st != TFX_OK) return st;
-    kern<<<grid, kAttnThreads, C::kSmemBytes, stream>>>(q, k, v, ld_qkv, out, ld_out, heads, seq,
-                                                         scale_log2, valid_len);
+    launch_pdl(kern, grid, dim3(kAttnThreads), C::kSmemBytes, stream, q, k, v, ld_qkv, out, ld_out,
+               heads, seq, scale_log2, valid_len);
   } else {
     auto kern = attention_mma_kernel<HD, false>;
     int st = ensure_smem(reinterpret_cast<const void*>(kern), C::kSmemBytes, done_n);
     if (st != TFX_OK) return st;
-    kern<<<grid, kAttnThreads, C::kSmemBytes, stream>>>(q, k, v, ld_qkv, out, ld_out, heads, seq,
-                                                         scale_log2, valid_len);
+    launch_pdl(kern, grid, dim3(kAttnThreads), C::kSmemBytes, stream, q, k, v, ld_qkv, out, ld_out,
+               heads, seq, scale_log2, valid_len);
   }
   return check_launch("attention_mma_kernel");
 }

@@ -95,6 +95,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         const __grid_constant__ CUtensorMap tm_v, __half* __restrict__ out,
                         int64_t ld_out, int heads, int seq, int nqb, float scale_log2,
                         const int32_t* __restrict__ valid_len, int* err) {
+  grid_dep_wait();
+  grid_dep_launch();
   using L = TcAttn<HD>;
   constexpr int S = L::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -473,6 +475,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 __global__ void __launch_bounds__(256)
     transpose_v_kernel(const __half* __restrict__ v, int64_t ld_qkv, __half* __restrict__ vt,
                        int64_t ld_vt, int seq, int cols) {
+  grid_dep_wait();
+  grid_dep_launch();
   __shared__ __align__(16) __half tile[64][64 + 8];
   const int s0 = blockIdx.x * 64, c0 = blockIdx.y * 64, b = blockIdx.z;
   for (int i = threadIdx.x; i < 64 * 8; i += blockDim.x) {
@@ -524,9 +528,8 @@ int launch_tc(const __half* q, const __half* k, const __half* v, int64_t ld_qkv,
   const int nqb = (seq + L::kNT * kTile - 1) / (L::kNT * kTile);
   const dim3 grid(static_cast<unsigned>(batch) * static_cast<unsigned>(heads),
                   static_cast<unsigned>(nqb));
-  kern<<<grid, kTcThreads, L::kSmem, stream>>>(tq, tk, tv, out, ld_out, heads, seq, nqb,
-                                                scale * 1.4426950408889634f, valid_len,
-                                                device_error_word());
+  launch_pdl(kern, grid, dim3(kTcThreads), L::kSmem, stream, tq, tk, tv, out, ld_out, heads, seq,
+             nqb, scale * 1.4426950408889634f, valid_len, device_error_word());
   return check_launch("attention_tc_kernel");
 }
 
@@ -574,7 +577,7 @@ int launch_transpose_v(const __half* v, int64_t ld_qkv, __half* vt, int batch, i
   const int64_t ld_vt = attention_vt_ld(seq);
   const dim3 grid(static_cast<unsigned>((ld_vt + 63) / 64), static_cast<unsigned>(cols / 64),
                   static_cast<unsigned>(batch));
-  transpose_v_kernel<<<grid, 256, 0, stream>>>(v, ld_qkv, vt, ld_vt, seq, cols);
+  launch_pdl(transpose_v_kernel, grid, dim3(256), 0, stream, v, ld_qkv, vt, ld_vt, seq, cols);
   return check_launch("transpose_v_kernel");
 }
 

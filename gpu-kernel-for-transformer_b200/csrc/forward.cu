@@ -19,12 +19,15 @@
 // adds an fp16-rounded update inside its LayerNorm kernel.
 // No allocation, no host synchronisation: graph-capturable.
 #include "internal.h"
+#include "ptx.cuh"
 
 namespace tfx {
 namespace {
 
 __global__ void zero_padded_rows_kernel(float* y, int seq, int d, const int32_t* valid_len,
                                         int64_t rows) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
   if (row >= rows) return;
   const int b = static_cast<int>(row / seq), s = static_cast<int>(row % seq);
@@ -198,7 +201,8 @@ int tfx_forward(const tfx_model* model, const float* x, float* y, int batch, int
   }
   if (valid_len != nullptr) {
     const int64_t blocks = (m + 7) / 8;
-    zero_padded_rows_kernel<<<blocks, 256, 0, stream>>>(y, seq, d, valid_len, m);
+    launch_pdl(zero_padded_rows_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream,
+               y, seq, d, valid_len, m);
     st = check_launch("zero_padded_rows_kernel");
   }
   return st;

@@ -343,6 +343,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     fence_mbar_init();
   }
+  grid_dep_wait();
+  grid_dep_launch();
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
@@ -894,7 +896,7 @@ int launch_fused_forward(const tfx_model* m, const float* x, float* y, int batch
     static int done[kMaxDevices] = {0};                                                         \
     st = ensure_smem(reinterpret_cast<const void*>(fused_forward_kernel<HDV>), kSmemBytes, done); \
     if (st != TFX_OK) return st;                                                                \
-    fused_forward_kernel<HDV><<<grid, kThreads, kSmemBytes, stream>>>(p);                       \
+    launch_pdl(fused_forward_kernel<HDV>, dim3(grid), dim3(kThreads), kSmemBytes, stream, p);  \
     break;                                                                                      \
   }
   switch (hd) {

@@ -78,6 +78,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     fence_mbar_init();
   }
+  grid_dep_wait();
+  grid_dep_launch();
   if (warp == 1) {
     tmem_alloc(tmem_slot, L::kTmemCols);
     tmem_relinquish();
@@ -278,9 +280,8 @@ int launch_gemm_t(const __half* a, int64_t lda, const __half* w, const float* bi
   if (st != TFX_OK) return st;
   const int64_t tiles = ((m + kBM - 1) / kBM) * (n / BN);
   const int grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
-  kern<<<grid, kThreads, L::kSmemBytes, stream>>>(tmA, tmW, bias, residual, out,
-                                                   static_cast<int>(m), n, k, ldr, ldo,
-                                                   device_error_word());
+  launch_pdl(kern, dim3(grid), dim3(kThreads), L::kSmemBytes, stream, tmA, tmW, bias, residual,
+             out, static_cast<int>(m), n, k, ldr, ldo, device_error_word());
   return check_launch("gemm_tc_kernel");
 }
 

@@ -20,6 +20,28 @@ int fail(int status, const char* fmt, ...);
 // Checks cudaGetLastError after a launch; maps a failure to TFX_ERR_CUDA.
 int check_launch(const char* what);
 
+// Launches `kern` with programmatic stream serialization: the kernel may be
+// scheduled while the previous kernel in the stream is still running, and
+// waits for it inside (grid_dep_wait in ptx.cuh) after its prologue, so the
+// launch latency and prologue overlap the predecessor's tail. Every kernel of
+// this library calls grid_dep_wait before its first global or TMEM access;
+// launches after a non-kernel operation (copy, event wait) are ordinary.
+template <typename... P, typename... A>
+inline cudaError_t launch_pdl(void (*kern)(P...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t stream, A&&... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<A&&>(args)...);
+}
+
 // Device error word (per device) the kernels write on a bounded-wait timeout.
 int* device_error_word();
 

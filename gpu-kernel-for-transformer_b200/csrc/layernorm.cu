@@ -40,6 +40,8 @@ __global__ void __launch_bounds__(32 * kRowsPerBlock)
                       const float* __restrict__ gamma, const float* __restrict__ beta,
                       float* residual_out, OutT* __restrict__ y, int64_t rows, int d, float eps,
                       int apply_affine) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kRowsPerBlock + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -104,11 +106,13 @@ int launch_nv(const float* x, const __half* u, const float* gamma, const float* 
               cudaStream_t stream) {
   const int64_t blocks = (rows + kRowsPerBlock - 1) / kRowsPerBlock;
   if (y_dtype == TFX_DTYPE_F16) {
-    layer_norm_kernel<NV, HAS_UPDATE, __half><<<blocks, 32 * kRowsPerBlock, 0, stream>>>(
-        x, u, gamma, beta, r_out, static_cast<__half*>(y), rows, d, eps, affine);
+    launch_pdl(layer_norm_kernel<NV, HAS_UPDATE, __half>, dim3(static_cast<unsigned>(blocks)),
+               dim3(32 * kRowsPerBlock), 0, stream, x, u, gamma, beta, r_out,
+               static_cast<__half*>(y), rows, d, eps, affine);
   } else {
-    layer_norm_kernel<NV, HAS_UPDATE, float><<<blocks, 32 * kRowsPerBlock, 0, stream>>>(
-        x, u, gamma, beta, r_out, static_cast<float*>(y), rows, d, eps, affine);
+    launch_pdl(layer_norm_kernel<NV, HAS_UPDATE, float>, dim3(static_cast<unsigned>(blocks)),
+               dim3(32 * kRowsPerBlock), 0, stream, x, u, gamma, beta, r_out,
+               static_cast<float*>(y), rows, d, eps, affine);
   }
   return check_launch("layer_norm_kernel");
 }

@@ -36,6 +36,22 @@ __device__ __forceinline__ void record_error(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
 }
 
+// ------------------------------------------- programmatic dependent launch
+// Blocks until the previous grid in the stream has completed and its memory
+// is visible (returns at once when there is none). Called by every thread of
+// every kernel before its first global-memory access and before TMEM is
+// allocated: a CTA that holds TMEM then never waits on an earlier grid, so
+// an earlier grid's CTA sharing the SM always gets its TMEM and finishes.
+__device__ __forceinline__ void grid_dep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// Lets the next grid in the stream be scheduled (it still waits for this
+// grid's completion in its own grid_dep_wait).
+__device__ __forceinline__ void grid_dep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
