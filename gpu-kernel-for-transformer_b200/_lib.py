@@ -53,6 +53,8 @@ SIGNATURES = {
     "tfx_forward_workspace_bytes": (_I64, [_P, _I, _I]),
     "tfx_forward": (_I, [_P, _P, _P, _I, _I, _P, _P, ctypes.c_size_t, _P]),
     "tfx_forward_static": (_I, [_P, _P, _P, _I, _I, _P, _P]),
+    "tfx_forward_kv_workspace_bytes": (_I64, [_P, _I, _I]),
+    "tfx_forward_kv": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _P, _P, ctypes.c_size_t, _P]),
     "tfx_read_device_error": (_I, [ctypes.POINTER(_I)]),
 }
 

@@ -74,9 +74,9 @@ struct AttnCfg {
 
 template <int HD, bool CAUSAL>
 __global__ void __launch_bounds__(kAttnThreads)
-    attention_mma_kernel(const __half* __restrict__ q, const __half* __restrict__ k,
-                         const __half* __restrict__ v, int64_t ld_qkv, __half* __restrict__ out,
-                         int64_t ld_out, int heads, int seq, float scale_log2,
+    attention_mma_kernel(const __half* __restrict__ q, int64_t ld_q, const __half* __restrict__ k,
+                         const __half* __restrict__ v, AttnKv kv, __half* __restrict__ out,
+                         int64_t ld_out, int heads, int q_len, float scale_log2,
                          const int32_t* __restrict__ valid_len) {
   grid_dep_wait();
   grid_dep_launch();
@@ -90,13 +90,15 @@ __global__ void __launch_bounds__(kAttnThreads)
   __half* sV = sK + 2 * C::kKElems;  // 2 buffers
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int nqb = (seq + kBQ - 1) / kBQ;
+  const int nqb = (q_len + kBQ - 1) / kBQ;
   const int qb = CAUSAL ? (nqb - 1 - static_cast<int>(blockIdx.x)) : static_cast<int>(blockIdx.x);
   const int h = blockIdx.y, b = blockIdx.z;
   const int q0 = qb * kBQ;
-  const int64_t row0 = static_cast<int64_t>(b) * seq;
-  const int klen = valid_len ? min(seq, max(0, valid_len[b])) : seq;
-  int kend = CAUSAL ? min(klen, q0 + kBQ) : klen;
+  const int64_t row0 = static_cast<int64_t>(b) * q_len;      // queries and outputs
+  const int64_t kv_row0 = static_cast<int64_t>(b) * kv.batch_rows;
+  // Query row i sits at key position kv.q_off + i; causal rows see keys up to it.
+  const int klen = valid_len ? min(kv.len, max(0, valid_len[b])) : kv.len;
+  int kend = CAUSAL ? min(klen, kv.q_off + q0 + kBQ) : klen;
   const int nkb = (kend + BKV - 1) / BKV;
 
   // Zero the reduction padding columns once (HD < 16 only).
@@ -112,8 +114,8 @@ __global__ void __launch_bounds__(kAttnThreads)
   for (int i = tid; i < kBQ * CH; i += kAttnThreads) {
     const int r = i / CH, c = i % CH;
     const int qi = q0 + r;
-    const bool ok = qi < seq;
-    const __half* src = q + (row0 + (ok ? qi : 0)) * ld_qkv + h * HD + c * 8;
+    const bool ok = qi < q_len;
+    const __half* src = q + (row0 + (ok ? qi : 0)) * ld_q + h * HD + c * 8;
     cp_async16(smem_u32(sQ + r * C::kQStride + c * 8), src, ok);
   }
   auto load_kv = [&](int kb, int buf) {
@@ -122,7 +124,7 @@ __global__ void __launch_bounds__(kAttnThreads)
       const int r = i / CH, c = i % CH;
       const int ki = k0 + r;
       const bool ok = ki < kend;
-      const int64_t off = (row0 + (ok ? ki : 0)) * ld_qkv + h * HD + c * 8;
+      const int64_t off = (kv_row0 + (ok ? ki : 0)) * kv.ld + h * HD + c * 8;
       cp_async16(smem_u32(sK + buf * C::kKElems + r * C::kKStride + c * 8), k + off, ok);
       cp_async16(smem_u32(sV + buf * C::kVElems + r * C::kVStride + c * 8), v + off, ok);
     }
@@ -137,6 +139,7 @@ __global__ void __launch_bounds__(kAttnThreads)
   float l_run[2] = {0.f, 0.f};
   const int g = lane >> 2, t = lane & 3;
   const int qrow_a = q0 + warp * 16 + g;  // rows owned: qrow_a and qrow_a + 8
+  const int qpos_a = kv.q_off + qrow_a;   // their key positions
 
   for (int kb = 0; kb < nkb; ++kb) {
     const int buf = kb & 1;
@@ -168,7 +171,8 @@ __global__ void __launch_bounds__(kAttnThreads)
     }
     // ---- mask + online softmax (log2 domain)
     const int k0 = kb * BKV;
-    const bool need_mask = (k0 + BKV > kend) || (CAUSAL && k0 + BKV - 1 > q0 + warp * 16);
+    const bool need_mask =
+        (k0 + BKV > kend) || (CAUSAL && k0 + BKV - 1 > kv.q_off + q0 + warp * 16);
     float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
     for (int j = 0; j < NT_S; ++j) {
@@ -177,7 +181,7 @@ __global__ void __launch_bounds__(kAttnThreads)
         float val = s[j][e] * scale_log2;
         if (need_mask) {
           const int key = k0 + j * 8 + 2 * t + (e & 1);
-          const int qr = qrow_a + (e >> 1) * 8;
+          const int qr = qpos_a + (e >> 1) * 8;
           if (key >= kend || (CAUSAL && key > qr)) val = -INFINITY;
         }
         s[j][e] = val;
@@ -254,38 +258,66 @@ __global__ void __launch_bounds__(kAttnThreads)
 #pragma unroll
   for (int i = 0; i < NT_O; ++i) {
     const int col = h * HD + i * 8 + 2 * t;
-    if (qrow_a < seq)
+    if (qrow_a < q_len)
       *reinterpret_cast<uint32_t*>(out + (row0 + qrow_a) * ld_out + col) =
           pack_half2(o[i][0] * inv0, o[i][1] * inv0);
-    if (qrow_a + 8 < seq)
+    if (qrow_a + 8 < q_len)
       *reinterpret_cast<uint32_t*>(out + (row0 + qrow_a + 8) * ld_out + col) =
           pack_half2(o[i][2] * inv1, o[i][3] * inv1);
   }
 }
 
 template <int HD>
-int launch_hd(const __half* q, const __half* k, const __half* v, int64_t ld_qkv, __half* out,
-              int64_t ld_out, int batch, int heads, int seq, float scale, int causal,
-              const int32_t* valid_len, cudaStream_t stream) {
+int launch_hd(const __half* q, int64_t ld_q, const __half* k, const __half* v, const AttnKv& kv,
+              __half* out, int64_t ld_out, int batch, int heads, int q_len, float scale,
+              int causal, const int32_t* valid_len, cudaStream_t stream) {
   using C = AttnCfg<HD>;
   static int done_c[kMaxDevices] = {0};
   static int done_n[kMaxDevices] = {0};
   const float scale_log2 = scale * 1.4426950408889634f;
-  dim3 grid((seq + kBQ - 1) / kBQ, heads, batch);
+  dim3 grid((q_len + kBQ - 1) / kBQ, heads, batch);
   if (causal) {
     auto kern = attention_mma_kernel<HD, true>;
     int st = ensure_smem(reinterpret_cast<const void*>(kern), C::kSmemBytes, done_c);
     if (st != TFX_OK) return st;
-    launch_pdl(kern, grid, dim3(kAttnThreads), C::kSmemBytes, stream, q, k, v, ld_qkv, out, ld_out,
-               heads, seq, scale_log2, valid_len);
+    launch_pdl(kern, grid, dim3(kAttnThreads), C::kSmemBytes, stream, q, ld_q, k, v, kv, out,
+               ld_out, heads, q_len, scale_log2, valid_len);
   } else {
     auto kern = attention_mma_kernel<HD, false>;
     int st = ensure_smem(reinterpret_cast<const void*>(kern), C::kSmemBytes, done_n);
     if (st != TFX_OK) return st;
-    launch_pdl(kern, grid, dim3(kAttnThreads), C::kSmemBytes, stream, q, k, v, ld_qkv, out, ld_out,
-               heads, seq, scale_log2, valid_len);
+    launch_pdl(kern, grid, dim3(kAttnThreads), C::kSmemBytes, stream, q, ld_q, k, v, kv, out,
+               ld_out, heads, q_len, scale_log2, valid_len);
   }
   return check_launch("attention_mma_kernel");
+}
+
+int launch_mma(const __half* q, int64_t ld_q, const __half* k, const __half* v, const AttnKv& kv,
+               __half* out, int64_t ld_out, int batch, int heads, int q_len, int head_dim,
+               float scale, int causal, const int32_t* valid_len, cudaStream_t stream) {
+  switch (head_dim) {
+    case 8:
+      return launch_hd<8>(q, ld_q, k, v, kv, out, ld_out, batch, heads, q_len, scale, causal,
+                          valid_len, stream);
+    case 16:
+      return launch_hd<16>(q, ld_q, k, v, kv, out, ld_out, batch, heads, q_len, scale, causal,
+                           valid_len, stream);
+    case 32:
+      return launch_hd<32>(q, ld_q, k, v, kv, out, ld_out, batch, heads, q_len, scale, causal,
+                           valid_len, stream);
+    case 64:
+      return launch_hd<64>(q, ld_q, k, v, kv, out, ld_out, batch, heads, q_len, scale, causal,
+                           valid_len, stream);
+    case 128:
+      return launch_hd<128>(q, ld_q, k, v, kv, out, ld_out, batch, heads, q_len, scale, causal,
+                            valid_len, stream);
+    case 256:
+      return launch_hd<256>(q, ld_q, k, v, kv, out, ld_out, batch, heads, q_len, scale, causal,
+                            valid_len, stream);
+    default:
+      return fail(TFX_ERR_UNSUPPORTED, "tfx_attention: head_dim %d not in {8,16,32,64,128,256}",
+                  head_dim);
+  }
 }
 
 }  // namespace
@@ -293,33 +325,22 @@ int launch_hd(const __half* q, const __half* k, const __half* v, int64_t ld_qkv,
 int launch_attention(const __half* q, const __half* k, const __half* v, int64_t ld_qkv,
                      __half* out, int64_t ld_out, int batch, int heads, int seq, int head_dim,
                      float scale, int causal, const int32_t* valid_len, cudaStream_t stream) {
-  // Head dims 64 and 128 run on the tcgen05 kernel (attention_tc.cu).
+  // Head dims 64, 128 and 256 run on the tcgen05 kernel (attention_tc.cu).
   if (attention_tc_supported(head_dim, scale))
     return launch_attention_tc(q, k, v, ld_qkv, out, ld_out, batch, heads, seq, head_dim, scale,
                                causal, valid_len, stream);
-  switch (head_dim) {
-    case 8:
-      return launch_hd<8>(q, k, v, ld_qkv, out, ld_out, batch, heads, seq, scale, causal,
-                          valid_len, stream);
-    case 16:
-      return launch_hd<16>(q, k, v, ld_qkv, out, ld_out, batch, heads, seq, scale, causal,
-                           valid_len, stream);
-    case 32:
-      return launch_hd<32>(q, k, v, ld_qkv, out, ld_out, batch, heads, seq, scale, causal,
-                           valid_len, stream);
-    case 64:
-      return launch_hd<64>(q, k, v, ld_qkv, out, ld_out, batch, heads, seq, scale, causal,
-                           valid_len, stream);
-    case 128:
-      return launch_hd<128>(q, k, v, ld_qkv, out, ld_out, batch, heads, seq, scale, causal,
-                            valid_len, stream);
-    case 256:
-      return launch_hd<256>(q, k, v, ld_qkv, out, ld_out, batch, heads, seq, scale, causal,
-                            valid_len, stream);
-    default:
-      return fail(TFX_ERR_UNSUPPORTED, "tfx_attention: head_dim %d not in {8,16,32,64,128,256}",
-                  head_dim);
-  }
+  return launch_mma(q, ld_qkv, k, v, AttnKv{ld_qkv, seq, seq, 0}, out, ld_out, batch, heads, seq,
+                    head_dim, scale, causal, valid_len, stream);
+}
+
+int launch_attention_kv(const __half* q, int64_t ld_q, const __half* k, const __half* v,
+                        const AttnKv& kv, __half* out, int64_t ld_out, int batch, int heads,
+                        int q_len, int head_dim, float scale, cudaStream_t stream) {
+  if (attention_tc_supported(head_dim, scale))
+    return launch_attention_tc_kv(q, ld_q, k, v, kv, out, ld_out, batch, heads, q_len, head_dim,
+                                  scale, stream);
+  return launch_mma(q, ld_q, k, v, kv, out, ld_out, batch, heads, q_len, head_dim, scale, 1,
+                    nullptr, stream);
 }
 
 }  // namespace tfx

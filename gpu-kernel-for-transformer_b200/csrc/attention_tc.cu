@@ -93,8 +93,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                         const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v, __half* __restrict__ out,
-                        int64_t ld_out, int heads, int seq, int nqb, float scale_log2,
-                        const int32_t* __restrict__ valid_len, int* err) {
+                        int64_t ld_out, int heads, int q_len, int nqb, int kv_len, int q_off,
+                        float scale_log2, const int32_t* __restrict__ valid_len, int* err) {
   grid_dep_wait();
   grid_dep_launch();
   using L = TcAttn<HD>;
@@ -123,10 +123,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   // Causal: the heaviest query blocks (the last ones) are launched first.
   const int qb = CAUSAL ? nqb - 1 - static_cast<int>(blockIdx.y) : static_cast<int>(blockIdx.y);
   const int q0 = qb * L::kNT * kTile;
-  const int kend = valid_len ? min(seq, max(0, valid_len[b])) : seq;
+  // Query row i of this sequence sits at key position q_off + i (q_off > 0:
+  // new tokens attending a KV cache); causal rows see keys <= their position.
+  const int kend = valid_len ? min(kv_len, max(0, valid_len[b])) : kv_len;
   auto tiles_for = [&](int qx) {
-    if (qx >= seq) return 0;
-    const int lim = CAUSAL ? min(kend, qx + kTile) : kend;
+    if (qx >= q_len) return 0;
+    const int lim = CAUSAL ? min(kend, q_off + qx + kTile) : kend;
     return (lim + kTile - 1) / kTile;
   };
   const int nA = tiles_for(q0);
@@ -323,8 +325,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const uint32_t t_s = tmem + lane_off + x * kTile;
     const uint32_t t_p = tmem + lane_off + L::kColP + x * L::kPStride;
     const uint32_t t_o = tmem + lane_off + L::kColO + x * HD;
-    const int lim_row = CAUSAL ? min(kend, q + 1) : kend;    // keys [0, lim_row) visible
-    const int lim_tile = CAUSAL ? min(kend, qx + 1) : kend;  // smallest lim_row of the tile
+    const int lim_row = CAUSAL ? min(kend, q_off + q + 1) : kend;  // keys [0, lim_row) visible
+    const int lim_tile = CAUSAL ? min(kend, q_off + qx + 1) : kend;  // smallest of the tile
     float m_ref = 0.f;
     uint64_t lsum0 = 0, lsum1 = 0;
     bool ok = true;
@@ -434,7 +436,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     f2_unpack(lsum1, lc, ld);
     const float l = (la + lb) + (lc + ld);
     const float inv = l > 0.f ? 1.f / l : 0.f;
-    __half* dst = out + (static_cast<int64_t>(b) * seq + q) * ld_out + h * HD;
+    __half* dst = out + (static_cast<int64_t>(b) * q_len + q) * ld_out + h * HD;
     if (ok && nx > 0) {
       tc_fence_after();
 #pragma unroll 1
@@ -442,7 +444,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         uint32_t o[32];
         tmem_ld32(t_o + c, o);
         tmem_ld_wait();
-        if (q < seq) {
+        if (q < q_len) {
           uint4* d4 = reinterpret_cast<uint4*>(dst + c);
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
@@ -452,7 +454,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
         }
       }
-    } else if (ok && q < seq) {
+    } else if (ok && q < q_len) {
       // No visible key (valid_len 0): the output row is zero.
       uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
@@ -500,60 +502,69 @@ __global__ void __launch_bounds__(256)
 }
 
 template <int HD, bool CAUSAL, bool VT>
-int launch_tc(const __half* q, const __half* k, const __half* v, int64_t ld_qkv, int64_t ld_vt,
-              __half* out, int64_t ld_out, int batch, int heads, int seq, float scale,
-              const int32_t* valid_len, cudaStream_t stream) {
+int launch_tc(const __half* q, int64_t ld_q, const __half* k, const __half* v, int64_t ld_vt,
+              __half* out, int64_t ld_out, int batch, int heads, int q_len, const AttnKv& kv,
+              float scale, const int32_t* valid_len, cudaStream_t stream) {
   using L = TcAttn<HD>;
   static int smem_done[kMaxDevices] = {0};
   auto kern = attention_tc_kernel<HD, CAUSAL, VT>;
   int st = ensure_smem(reinterpret_cast<const void*>(kern), L::kSmem, smem_done);
   if (st != TFX_OK) return st;
   const uint64_t cols = static_cast<uint64_t>(heads) * HD;
-  const uint64_t bstride = static_cast<uint64_t>(seq) * static_cast<uint64_t>(ld_qkv);
+  const uint64_t kv_len = static_cast<uint64_t>(kv.len);
+  const uint64_t kv_bstride = static_cast<uint64_t>(kv.batch_rows) * static_cast<uint64_t>(kv.ld);
   CUtensorMap tq, tk, tv;
-  st = make_tmap_3d(&tq, q, static_cast<uint64_t>(seq), static_cast<uint64_t>(batch), cols,
-                    static_cast<uint64_t>(ld_qkv), bstride, 64, kTile);
+  // K/V rows at or past kv.len read as zeros (TMA out-of-bounds fill), so a
+  // partly used last tile never multiplies a masked score by stale data.
+  st = make_tmap_3d(&tq, q, static_cast<uint64_t>(q_len), static_cast<uint64_t>(batch), cols,
+                    static_cast<uint64_t>(ld_q),
+                    static_cast<uint64_t>(q_len) * static_cast<uint64_t>(ld_q), 64, kTile);
   if (st == TFX_OK)
-    st = make_tmap_3d(&tk, k, static_cast<uint64_t>(seq), static_cast<uint64_t>(batch), cols,
-                      static_cast<uint64_t>(ld_qkv), bstride, 64, kTile);
+    st = make_tmap_3d(&tk, k, kv_len, static_cast<uint64_t>(batch), cols,
+                      static_cast<uint64_t>(kv.ld), kv_bstride, 64, kTile);
   if (st == TFX_OK) {
-    if (VT)  // [batch][cols][ld_vt]: keys innermost, keys >= seq read as zeros
-      st = make_tmap_3d(&tv, v, cols, static_cast<uint64_t>(batch), static_cast<uint64_t>(seq),
+    if (VT)  // [batch][cols][ld_vt]: keys innermost, keys >= kv.len read as zeros
+      st = make_tmap_3d(&tv, v, cols, static_cast<uint64_t>(batch), kv_len,
                         static_cast<uint64_t>(ld_vt), cols * static_cast<uint64_t>(ld_vt), 64, HD);
     else
-      st = make_tmap_3d(&tv, v, static_cast<uint64_t>(seq), static_cast<uint64_t>(batch), cols,
-                        static_cast<uint64_t>(ld_qkv), bstride, 64, kTile);
+      st = make_tmap_3d(&tv, v, kv_len, static_cast<uint64_t>(batch), cols,
+                        static_cast<uint64_t>(kv.ld), kv_bstride, 64, kTile);
   }
   if (st != TFX_OK) return st;
-  const int nqb = (seq + L::kNT * kTile - 1) / (L::kNT * kTile);
+  const int nqb = (q_len + L::kNT * kTile - 1) / (L::kNT * kTile);
   const dim3 grid(static_cast<unsigned>(batch) * static_cast<unsigned>(heads),
                   static_cast<unsigned>(nqb));
-  launch_pdl(kern, grid, dim3(kTcThreads), L::kSmem, stream, tq, tk, tv, out, ld_out, heads, seq,
-             nqb, scale * 1.4426950408889634f, valid_len, device_error_word());
+  launch_pdl(kern, grid, dim3(kTcThreads), L::kSmem, stream, tq, tk, tv, out, ld_out, heads, q_len,
+             nqb, kv.len, kv.q_off, scale * 1.4426950408889634f, valid_len, device_error_word());
   return check_launch("attention_tc_kernel");
 }
 
-template <bool VT>
-int dispatch_tc(const __half* q, const __half* k, const __half* v, int64_t ld_qkv, int64_t ld_vt,
-                __half* out, int64_t ld_out, int batch, int heads, int seq, int head_dim,
+template <int HD, bool VT>
+int launch_tc_c(const __half* q, int64_t ld_q, const __half* k, const __half* v, int64_t ld_vt,
+                __half* out, int64_t ld_out, int batch, int heads, int q_len, const AttnKv& kv,
                 float scale, int causal, const int32_t* valid_len, cudaStream_t stream) {
-  if (static_cast<int64_t>(batch) * heads > 0x7fffffff || (seq + kTile - 1) / kTile > 65535)
+  return causal ? launch_tc<HD, true, VT>(q, ld_q, k, v, ld_vt, out, ld_out, batch, heads, q_len,
+                                          kv, scale, valid_len, stream)
+                : launch_tc<HD, false, VT>(q, ld_q, k, v, ld_vt, out, ld_out, batch, heads, q_len,
+                                           kv, scale, valid_len, stream);
+}
+
+template <bool VT>
+int dispatch_tc(const __half* q, int64_t ld_q, const __half* k, const __half* v, int64_t ld_vt,
+                __half* out, int64_t ld_out, int batch, int heads, int q_len, const AttnKv& kv,
+                int head_dim, float scale, int causal, const int32_t* valid_len,
+                cudaStream_t stream) {
+  if (static_cast<int64_t>(batch) * heads > 0x7fffffff || (q_len + kTile - 1) / kTile > 65535)
     return fail(TFX_ERR_UNSUPPORTED, "tfx_attention: batch*heads or seq too large for the grid");
   if (head_dim == 64)
-    return causal ? launch_tc<64, true, VT>(q, k, v, ld_qkv, ld_vt, out, ld_out, batch, heads,
-                                            seq, scale, valid_len, stream)
-                  : launch_tc<64, false, VT>(q, k, v, ld_qkv, ld_vt, out, ld_out, batch, heads,
-                                             seq, scale, valid_len, stream);
+    return launch_tc_c<64, VT>(q, ld_q, k, v, ld_vt, out, ld_out, batch, heads, q_len, kv, scale,
+                               causal, valid_len, stream);
   if (head_dim == 128)
-    return causal ? launch_tc<128, true, VT>(q, k, v, ld_qkv, ld_vt, out, ld_out, batch, heads,
-                                             seq, scale, valid_len, stream)
-                  : launch_tc<128, false, VT>(q, k, v, ld_qkv, ld_vt, out, ld_out, batch, heads,
-                                              seq, scale, valid_len, stream);
+    return launch_tc_c<128, VT>(q, ld_q, k, v, ld_vt, out, ld_out, batch, heads, q_len, kv, scale,
+                                causal, valid_len, stream);
   if (head_dim == 256)
-    return causal ? launch_tc<256, true, VT>(q, k, v, ld_qkv, ld_vt, out, ld_out, batch, heads,
-                                             seq, scale, valid_len, stream)
-                  : launch_tc<256, false, VT>(q, k, v, ld_qkv, ld_vt, out, ld_out, batch, heads,
-                                              seq, scale, valid_len, stream);
+    return launch_tc_c<256, VT>(q, ld_q, k, v, ld_vt, out, ld_out, batch, heads, q_len, kv, scale,
+                                causal, valid_len, stream);
   return fail(TFX_ERR_UNSUPPORTED, "attention_tc: head_dim %d not in {64,128,256}", head_dim);
 }
 
@@ -566,8 +577,9 @@ bool attention_tc_supported(int head_dim, float scale) {
 int launch_attention_tc(const __half* q, const __half* k, const __half* v, int64_t ld_qkv,
                         __half* out, int64_t ld_out, int batch, int heads, int seq, int head_dim,
                         float scale, int causal, const int32_t* valid_len, cudaStream_t stream) {
-  return dispatch_tc<false>(q, k, v, ld_qkv, 0, out, ld_out, batch, heads, seq, head_dim, scale,
-                            causal, valid_len, stream);
+  return dispatch_tc<false>(q, ld_qkv, k, v, 0, out, ld_out, batch, heads, seq,
+                            AttnKv{ld_qkv, seq, seq, 0}, head_dim, scale, causal, valid_len,
+                            stream);
 }
 
 int64_t attention_vt_ld(int seq) { return (static_cast<int64_t>(seq) + 7) / 8 * 8; }
@@ -581,12 +593,20 @@ int launch_transpose_v(const __half* v, int64_t ld_qkv, __half* vt, int batch, i
   return check_launch("transpose_v_kernel");
 }
 
+int launch_attention_tc_kv(const __half* q, int64_t ld_q, const __half* k, const __half* v,
+                           const AttnKv& kv, __half* out, int64_t ld_out, int batch, int heads,
+                           int q_len, int head_dim, float scale, cudaStream_t stream) {
+  return dispatch_tc<false>(q, ld_q, k, v, 0, out, ld_out, batch, heads, q_len, kv, head_dim,
+                            scale, 1, nullptr, stream);
+}
+
 int launch_attention_tc_vt(const __half* q, const __half* k, const __half* vt, int64_t ld_qkv,
                            __half* out, int64_t ld_out, int batch, int heads, int seq,
                            int head_dim, float scale, int causal, const int32_t* valid_len,
                            cudaStream_t stream) {
-  return dispatch_tc<true>(q, k, vt, ld_qkv, attention_vt_ld(seq), out, ld_out, batch, heads,
-                           seq, head_dim, scale, causal, valid_len, stream);
+  return dispatch_tc<true>(q, ld_qkv, k, vt, attention_vt_ld(seq), out, ld_out, batch, heads, seq,
+                           AttnKv{ld_qkv, seq, seq, 0}, head_dim, scale, causal, valid_len,
+                           stream);
 }
 
 }  // namespace tfx

@@ -36,6 +36,29 @@ __global__ void zero_padded_rows_kernel(float* y, int seq, int d, const int32_t*
   for (int c = threadIdx.x & 31; c < d / 4; c += 32) yr[c] = make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
+// KV cache append: the K and V thirds of each new token's packed projection
+// row -> its position in the layer's caches ([batch][capacity][d] each).
+// A warp per token row, 16-byte accesses.
+__global__ void kv_append_kernel(const __half* __restrict__ qkv, int64_t ld_qkv,
+                                 __half* __restrict__ k_cache, __half* __restrict__ v_cache,
+                                 int new_tokens, int d, int capacity, int cache_len,
+                                 int64_t rows) {
+  grid_dep_wait();
+  grid_dep_launch();
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int64_t b = row / new_tokens, t = row % new_tokens;
+  const int64_t dst = (b * capacity + cache_len + t) * d;
+  const uint4* sk = reinterpret_cast<const uint4*>(qkv + row * ld_qkv + d);
+  const uint4* sv = reinterpret_cast<const uint4*>(qkv + row * ld_qkv + 2 * d);
+  uint4* dk = reinterpret_cast<uint4*>(k_cache + dst);
+  uint4* dv = reinterpret_cast<uint4*>(v_cache + dst);
+  for (int c = threadIdx.x & 31; c < d / 8; c += 32) {
+    dk[c] = sk[c];
+    dv[c] = sv[c];
+  }
+}
+
 constexpr size_t kAlign = 256;
 int g_fused_policy = 1;  // 1: fused whole-forward kernel where it applies; 0: per-op chain
 
@@ -108,57 +131,28 @@ int check_model(const tfx_model* mdl) {
   return TFX_OK;
 }
 
-}  // namespace
-}  // namespace tfx
+// Caller-owned KV caches of an incremental forward: fp16 [layers][batch]
+// [capacity][d] each; positions < cache_len hold earlier tokens.
+struct KvCache {
+  __half* k;
+  __half* v;
+  int capacity;
+  int cache_len;
+};
 
-using namespace tfx;
-
-extern "C" {
-
-int tfx_set_fused_policy(int enable) {
-  const int prev = g_fused_policy;
-  g_fused_policy = enable ? 1 : 0;
-  return prev;
-}
-
-int64_t tfx_forward_workspace_bytes(const tfx_model* model, int batch, int seq) {
-  if (check_model(model) != TFX_OK || batch <= 0 || seq <= 0) return -1;
-  if (use_fused(model, seq, nullptr)) return 0;
-  return static_cast<int64_t>(plan_workspace(nullptr, batch, seq, model->d_model, model->ffn_dim,
-                                            model->d_model / model->num_heads)
-                                 .bytes);
-}
-
-int tfx_forward(const tfx_model* model, const float* x, float* y, int batch, int seq,
-                const int32_t* valid_len, void* workspace, size_t workspace_bytes,
-                tfx_stream_t stream_) {
-  int st = check_model(model);
-  if (st != TFX_OK) return st;
-  if (x == nullptr || y == nullptr)
-    return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward: null x or y");
-  if (batch <= 0 || seq <= 0)
-    return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward: batch and seq must be positive");
-  if (x == y) return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward: y must not alias x");
-  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(y) % 16 ||
-      reinterpret_cast<uintptr_t>(workspace) % kAlign)
-    return fail(TFX_ERR_MISALIGNED, "tfx_forward: x/y 16-byte and workspace 256-byte alignment");
-  if (use_fused(model, seq, valid_len))
-    return launch_fused_forward(model, x, y, batch, seq, valid_len,
-                                reinterpret_cast<cudaStream_t>(stream_));
-  if (workspace == nullptr)
-    return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward: null workspace");
+// The per-op chain over `seq` token rows per sequence. With `kv`, each
+// layer's new K/V rows are appended to its cache, and the new tokens attend
+// every cached key (positions before theirs: causal with an offset).
+int run_chain(const tfx_model* model, const float* x, float* y, int batch, int seq,
+              const int32_t* valid_len, const Workspace& ws, cudaStream_t stream,
+              const KvCache* kv) {
   const int64_t m = static_cast<int64_t>(batch) * seq;
   const int d = model->d_model, f = model->ffn_dim, nh = model->num_heads, hd = d / nh;
-  const Workspace ws = plan_workspace(static_cast<char*>(workspace), batch, seq, d, f, hd);
-  if (workspace_bytes < ws.bytes)
-    return fail(TFX_ERR_WORKSPACE, "tfx_forward: workspace %zu < required %zu bytes",
-                workspace_bytes, ws.bytes);
-  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   const float eps = model->eps;
   const float scale = 1.0f / sqrtf(static_cast<float>(hd));
 
-  st = launch_layer_norm(x, model->layers[0].norm1_weight, model->layers[0].norm1_bias, ws.h,
-                         TFX_DTYPE_F16, m, d, eps, 1, stream);
+  int st = launch_layer_norm(x, model->layers[0].norm1_weight, model->layers[0].norm1_bias, ws.h,
+                             TFX_DTYPE_F16, m, d, eps, 1, stream);
   if (st != TFX_OK) return st;
   for (int l = 0; l < model->num_layers; ++l) {
     const tfx_layer& L = model->layers[l];
@@ -166,7 +160,22 @@ int tfx_forward(const tfx_model* model, const float* x, float* y, int batch, int
     st = launch_linear(ws.h, d, wqkv, L.qkv_bias, nullptr, 0, ws.qkv, 3 * d, m, 3 * d, d,
                        TFX_EPI_BIAS, stream);
     if (st != TFX_OK) return st;
-    if (attention_reads_vt(hd)) {
+    if (kv != nullptr) {
+      const size_t layer_elems = static_cast<size_t>(batch) * kv->capacity * d;
+      __half* kc = kv->k + l * layer_elems;
+      __half* vc = kv->v + l * layer_elems;
+      launch_pdl(kv_append_kernel, dim3(static_cast<unsigned>((m + 7) / 8)), dim3(256), 0,
+                 stream, ws.qkv, static_cast<int64_t>(3 * d), kc, vc, seq, d, kv->capacity,
+                 kv->cache_len, m);
+      st = check_launch("kv_append_kernel");
+      if (st != TFX_OK) return st;
+    }
+    if (kv != nullptr && kv->cache_len > 0) {
+      const AttnKv geom{d, kv->capacity, kv->cache_len + seq, kv->cache_len};
+      const size_t layer_elems = static_cast<size_t>(batch) * kv->capacity * d;
+      st = launch_attention_kv(ws.qkv, 3 * d, kv->k + l * layer_elems, kv->v + l * layer_elems,
+                               geom, ws.ctx, d, batch, nh, seq, hd, scale, stream);
+    } else if (attention_reads_vt(hd)) {
       st = launch_transpose_v(ws.qkv + 2 * d, 3 * d, ws.h, batch, seq, d, stream);
       if (st != TFX_OK) return st;
       st = launch_attention_tc_vt(ws.qkv, ws.qkv + d, ws.h, 3 * d, ws.ctx, d, batch, nh, seq, hd,
@@ -206,6 +215,95 @@ int tfx_forward(const tfx_model* model, const float* x, float* y, int batch, int
     st = check_launch("zero_padded_rows_kernel");
   }
   return st;
+}
+
+
+}  // namespace
+}  // namespace tfx
+
+using namespace tfx;
+
+extern "C" {
+
+int tfx_set_fused_policy(int enable) {
+  const int prev = g_fused_policy;
+  g_fused_policy = enable ? 1 : 0;
+  return prev;
+}
+
+int64_t tfx_forward_workspace_bytes(const tfx_model* model, int batch, int seq) {
+  if (check_model(model) != TFX_OK || batch <= 0 || seq <= 0) return -1;
+  if (use_fused(model, seq, nullptr)) return 0;
+  return static_cast<int64_t>(plan_workspace(nullptr, batch, seq, model->d_model, model->ffn_dim,
+                                            model->d_model / model->num_heads)
+                                 .bytes);
+}
+
+int tfx_forward(const tfx_model* model, const float* x, float* y, int batch, int seq,
+                const int32_t* valid_len, void* workspace, size_t workspace_bytes,
+                tfx_stream_t stream_) {
+  int st = check_model(model);
+  if (st != TFX_OK) return st;
+  if (x == nullptr || y == nullptr)
+    return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward: null x or y");
+  if (batch <= 0 || seq <= 0)
+    return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward: batch and seq must be positive");
+  if (x == y) return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward: y must not alias x");
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(y) % 16 ||
+      reinterpret_cast<uintptr_t>(workspace) % kAlign)
+    return fail(TFX_ERR_MISALIGNED, "tfx_forward: x/y 16-byte and workspace 256-byte alignment");
+  if (use_fused(model, seq, valid_len))
+    return launch_fused_forward(model, x, y, batch, seq, valid_len,
+                                reinterpret_cast<cudaStream_t>(stream_));
+  if (workspace == nullptr)
+    return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward: null workspace");
+  const int d = model->d_model, f = model->ffn_dim, hd = d / model->num_heads;
+  const Workspace ws = plan_workspace(static_cast<char*>(workspace), batch, seq, d, f, hd);
+  if (workspace_bytes < ws.bytes)
+    return fail(TFX_ERR_WORKSPACE, "tfx_forward: workspace %zu < required %zu bytes",
+                workspace_bytes, ws.bytes);
+  return run_chain(model, x, y, batch, seq, valid_len, ws, reinterpret_cast<cudaStream_t>(stream_),
+                   nullptr);
+}
+
+int64_t tfx_forward_kv_workspace_bytes(const tfx_model* model, int batch, int new_tokens) {
+  if (check_model(model) != TFX_OK || batch <= 0 || new_tokens <= 0) return -1;
+  return static_cast<int64_t>(plan_workspace(nullptr, batch, new_tokens, model->d_model,
+                                            model->ffn_dim, model->d_model / model->num_heads)
+                                 .bytes);
+}
+
+int tfx_forward_kv(const tfx_model* model, const float* x, float* y, int batch, int new_tokens,
+                   int cache_len, int capacity, void* k_cache, void* v_cache, void* workspace,
+                   size_t workspace_bytes, tfx_stream_t stream_) {
+  int st = check_model(model);
+  if (st != TFX_OK) return st;
+  if (!model->causal)
+    return fail(TFX_ERR_UNSUPPORTED, "tfx_forward_kv: KV caching requires a causal model");
+  if (x == nullptr || y == nullptr || k_cache == nullptr || v_cache == nullptr ||
+      workspace == nullptr)
+    return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward_kv: null pointer argument");
+  if (batch <= 0 || new_tokens <= 0 || cache_len < 0 || capacity <= 0)
+    return fail(TFX_ERR_INVALID_ARGUMENT,
+                "tfx_forward_kv: batch, new_tokens and capacity must be positive, cache_len >= 0");
+  if (static_cast<int64_t>(cache_len) + new_tokens > capacity)
+    return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward_kv: KV cache capacity exceeded (%lld > %d)",
+                static_cast<long long>(cache_len) + new_tokens, capacity);
+  if (x == y) return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward_kv: y must not alias x");
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(y) % 16 ||
+      reinterpret_cast<uintptr_t>(k_cache) % 16 || reinterpret_cast<uintptr_t>(v_cache) % 16 ||
+      reinterpret_cast<uintptr_t>(workspace) % kAlign)
+    return fail(TFX_ERR_MISALIGNED,
+                "tfx_forward_kv: x/y/caches 16-byte and workspace 256-byte alignment");
+  const int d = model->d_model, f = model->ffn_dim, hd = d / model->num_heads;
+  const Workspace ws = plan_workspace(static_cast<char*>(workspace), batch, new_tokens, d, f, hd);
+  if (workspace_bytes < ws.bytes)
+    return fail(TFX_ERR_WORKSPACE, "tfx_forward_kv: workspace %zu < required %zu bytes",
+                workspace_bytes, ws.bytes);
+  const KvCache kv{static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), capacity,
+                   cache_len};
+  return run_chain(model, x, y, batch, new_tokens, nullptr, ws,
+                   reinterpret_cast<cudaStream_t>(stream_), &kv);
 }
 
 }  // extern "C"

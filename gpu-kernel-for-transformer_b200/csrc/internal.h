@@ -79,6 +79,23 @@ int launch_attention(const __half* q, const __half* k, const __half* v, int64_t 
                      __half* out, int64_t ld_out, int batch, int heads, int seq, int head_dim,
                      float scale, int causal, const int32_t* valid_len, cudaStream_t stream);
 
+// Where an attention call's keys and values live relative to its queries.
+// Self-attention: interleaved with the queries ({ld_qkv, seq, seq, 0}). KV
+// cache: [batch][capacity][d] arrays of their own, the new tokens' queries
+// at key positions q_off .. q_off + q_len - 1.
+struct AttnKv {
+  int64_t ld;          // K/V row pitch (elements)
+  int64_t batch_rows;  // rows from one sequence's K/V to the next
+  int len;             // keys per sequence
+  int q_off;           // key position of query row 0 (causal: row i sees keys <= q_off + i)
+};
+
+// Causal attention of q_len new queries per sequence (row pitch ld_q,
+// sequences q_len rows apart) over kv.len cached keys; every head_dim.
+int launch_attention_kv(const __half* q, int64_t ld_q, const __half* k, const __half* v,
+                        const AttnKv& kv, __half* out, int64_t ld_out, int batch, int heads,
+                        int q_len, int head_dim, float scale, cudaStream_t stream);
+
 // tcgen05/TMEM flash attention for head_dim 64 and 128 (scale > 0).
 bool attention_tc_supported(int head_dim, float scale);
 int launch_attention_tc(const __half* q, const __half* k, const __half* v, int64_t ld_qkv,
@@ -90,6 +107,9 @@ int launch_attention_tc(const __half* q, const __half* k, const __half* v, int64
 int64_t attention_vt_ld(int seq);
 int launch_transpose_v(const __half* v, int64_t ld_qkv, __half* vt, int batch, int seq, int cols,
                        cudaStream_t stream);
+int launch_attention_tc_kv(const __half* q, int64_t ld_q, const __half* k, const __half* v,
+                           const AttnKv& kv, __half* out, int64_t ld_out, int batch, int heads,
+                           int q_len, int head_dim, float scale, cudaStream_t stream);
 int launch_attention_tc_vt(const __half* q, const __half* k, const __half* vt, int64_t ld_qkv,
                            __half* out, int64_t ld_out, int batch, int heads, int seq,
                            int head_dim, float scale, int causal, const int32_t* valid_len,

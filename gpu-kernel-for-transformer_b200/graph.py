@@ -107,6 +107,8 @@ def maybe_cuda_graph(model: nn.Module, x: torch.Tensor, valid_token_mask: Option
         return model, False, "disabled"
     if not x.is_cuda:
         return model, False, "CUDA Graphs require a CUDA input"
+    if bool(getattr(model, "_kv_cache_enabled", False)):
+        return model, False, "stateful KV-cache decoding uses the eager path"
     try:
         with torch.inference_mode():
             eager = model(x, valid_token_mask)

@@ -184,6 +184,8 @@ class UserOptimizedTransformer(BaselineTransformer):
         self._shape_execution_plan = _plan_for(config)
         self._mixed_precision_dtype: Optional[torch.dtype] = torch.float16
         self._kv_cache_enabled = False
+        self._kv_cache: Optional[Tuple[torch.Tensor, torch.Tensor]] = None
+        self._kv_cache_length = 0
         self._packed = None  # (key, tensors, ctypes structs)
         self._workspace: Dict[torch.device, torch.Tensor] = {}
         self._mask_cache = None
@@ -200,6 +202,8 @@ class UserOptimizedTransformer(BaselineTransformer):
         compute) is not provided by this implementation."""
         if dtype not in (None, torch.float16, torch.bfloat16):
             raise ValueError("mixed precision dtype must be float16 or bfloat16")
+        if self._kv_cache_length:
+            raise RuntimeError("reset the KV cache before changing precision")
         if dtype is None:
             raise NotImplementedError(
                 "the B200 path computes tensor-core operands in fp16; there is no FP32 path"
@@ -230,18 +234,75 @@ class UserOptimizedTransformer(BaselineTransformer):
             )
 
     def enable_kv_cache(self, enabled: bool = True) -> None:
-        """Incremental decoding (torch_transformer_benchmark.py:409-462) is not
-        part of this build's forward path."""
-        if enabled:
-            raise NotImplementedError("KV-cache decoding is not implemented in the B200 path")
-        self._kv_cache_enabled = False
+        """Incremental decoding (torch_transformer_benchmark.py:409-415):
+        each forward then takes the next chunk of tokens of the same
+        sequences, appends its keys/values to per-layer caches of capacity
+        ``config.seq_len`` and attends over everything cached so far."""
+        if enabled and not self.config.causal:
+            raise ValueError("KV caching requires a causal Transformer")
+        if enabled and self.training:
+            raise RuntimeError("call eval() before enabling the KV cache")
+        self._kv_cache_enabled = enabled
+        self.reset_kv_cache()
 
     def reset_kv_cache(self) -> None:
-        pass
+        """Clear cached keys and values before starting a new sequence
+        (torch_transformer_benchmark.py:417-420)."""
+        self._kv_cache = None
+        self._kv_cache_length = 0
 
     @property
     def kv_cache_length(self) -> int:
-        return 0
+        return self._kv_cache_length
+
+    def _kv_cache_for(self, x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+        """fp16 [layers, B, capacity, D] key and value caches, allocated on
+        first use (torch_transformer_benchmark.py:426-462)."""
+        cfg = self.config
+        shape = (cfg.num_layers, x.shape[0], cfg.seq_len, cfg.d_model)
+        c = self._kv_cache
+        if c is None:
+            c = (torch.empty(shape, dtype=torch.float16, device=x.device),
+                 torch.empty(shape, dtype=torch.float16, device=x.device))
+            self._kv_cache = c
+        elif c[0].shape != shape or c[0].device != x.device:
+            raise RuntimeError(
+                "KV cache does not match this input; reset it before changing "
+                "batch size, device, or dtype"
+            )
+        return c
+
+    def _forward_kv(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor]):
+        """One incremental step: x holds the next x.shape[1] tokens."""
+        if valid_token_mask is not None and not bool(valid_token_mask.all().item()):
+            raise ValueError("KV-cached decoding does not support padding")
+        batch, new_tokens, _ = x.shape
+        start = self._kv_cache_length
+        end = start + new_tokens
+        if end > self.config.seq_len:
+            raise ValueError(f"KV cache capacity exceeded ({end} > {self.config.seq_len})")
+        k_cache, v_cache = self._kv_cache_for(x)
+        _, _, _, model = self._prepare(x.device)
+        lib = _lib.load()
+        need = lib.tfx_forward_kv_workspace_bytes(ctypes.byref(model), batch, new_tokens)
+        if need < 0:
+            _lib.check(_lib.TFX_ERR_INVALID_ARGUMENT, "tfx_forward_kv_workspace_bytes")
+        ws = self._workspace.get(x.device)
+        if ws is None or ws.numel() < need:
+            ws = torch.empty(int(need), dtype=torch.uint8, device=x.device)
+            self._workspace[x.device] = ws
+        y = torch.empty_like(x)
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+        _lib.check(
+            lib.tfx_forward_kv(
+                ctypes.byref(model), x.data_ptr(), y.data_ptr(), batch, new_tokens, start,
+                self.config.seq_len, k_cache.data_ptr(), v_cache.data_ptr(), ws.data_ptr(),
+                ws.numel(), stream,
+            ),
+            "tfx_forward_kv",
+        )
+        self._kv_cache_length = end
+        return y
 
     # ---------------------------------------------------------- packing
     def _param_key(self, device: torch.device) -> Tuple:
@@ -347,6 +408,8 @@ class UserOptimizedTransformer(BaselineTransformer):
         self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None
     ) -> torch.Tensor:
         if x.device.type != "cuda":
+            if self._kv_cache_enabled:
+                raise RuntimeError("KV caching is implemented for CUDA inference")
             raise RuntimeError(
                 "UserOptimizedTransformer runs only on CUDA (sm_100a); there is no CPU fallback"
             )
@@ -355,6 +418,8 @@ class UserOptimizedTransformer(BaselineTransformer):
         if x.dtype != torch.float32:
             raise ValueError("x must be float32 (the residual stream is fp32)")
         x = x.contiguous()
+        if self._kv_cache_enabled:
+            return self._forward_kv(x, valid_token_mask)
         batch, seq, _ = x.shape
         valid_len = self._valid_lengths(x, valid_token_mask)
         _, _, _, model = self._prepare(x.device)

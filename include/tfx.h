@@ -213,6 +213,30 @@ TFX_API int tfx_forward_static(const tfx_model* model, const float* x, float* y,
                                int seq, const int32_t* valid_len, tfx_stream_t stream);
 
 /*
+ * KV-cached incremental forward of a causal model: replaces the reference's
+ * enable_kv_cache path (torch_transformer_benchmark.py:409-462 cache
+ * management and _append_kv_cache, 747-765 the new tokens' attention over
+ * the cache, 1085-1086 the length update).
+ * x, y: [batch, new_tokens, d_model] fp32, the tokens at positions
+ * cache_len .. cache_len + new_tokens - 1 of each sequence.
+ * k_cache, v_cache: caller-owned fp16 device arrays [num_layers][batch]
+ * [capacity][d_model] (16-byte aligned). Positions < cache_len hold the
+ * earlier tokens' keys / values; this call writes positions cache_len ..
+ * cache_len + new_tokens - 1 of every layer and leaves the rest untouched.
+ * Each new token attends every key at or before its own position.
+ * Errors: TFX_ERR_UNSUPPORTED for a non-causal model, TFX_ERR_INVALID_ARGUMENT
+ * when cache_len + new_tokens > capacity (the reference's "KV cache capacity
+ * exceeded"), TFX_ERR_WORKSPACE when the workspace is below
+ * tfx_forward_kv_workspace_bytes(model, batch, new_tokens).
+ */
+TFX_API int64_t tfx_forward_kv_workspace_bytes(const tfx_model* model, int batch,
+                                               int new_tokens);
+TFX_API int tfx_forward_kv(const tfx_model* model, const float* x, float* y, int batch,
+                           int new_tokens, int cache_len, int capacity, void* k_cache,
+                           void* v_cache, void* workspace, size_t workspace_bytes,
+                           tfx_stream_t stream);
+
+/*
  * Reads and clears the calling device's kernel error word (synchronises the
  * device). *code receives 0 or a timeout code; returns TFX_OK or TFX_ERR_CUDA.
  * No reference counterpart (the reference's kernels have no waits).

@@ -152,3 +152,48 @@ def test_transposed_v_entry_points_validate_on_the_host(lib):
                                 None) == L.TFX_ERR_UNSUPPORTED
     assert lib.tfx_attention_vt(None, 512, 768, 192, 1024, 64, 1, 1, 8, 64, 0.125, 1, None,
                                 None) == L.TFX_ERR_INVALID_ARGUMENT
+
+
+def _fake_model(L, d=128, h=4, f=128, layers=1, causal=1):
+    m = L.TfxModel()
+    m.d_model, m.num_heads, m.ffn_dim, m.num_layers = d, h, f, layers
+    arr = (L.TfxLayer * layers)()
+    for i in range(layers):
+        for name, _ in L.TfxLayer._fields_:
+            setattr(arr[i], name, 256)
+    m.layers = ctypes.cast(arr, ctypes.POINTER(L.TfxLayer))
+    m.final_norm_weight = m.final_norm_bias = 256
+    m.causal = causal
+    m.eps = 1e-5
+    return m, arr
+
+
+def test_kv_forward_validates_on_the_host(lib):
+    """tfx_forward_kv: the reference's KV-cache rules (causal only, capacity,
+    torch_transformer_benchmark.py:409-440) and the ABI's pointer rules,
+    all checked before anything is enqueued."""
+    pkg = load_package()
+    L = pkg._lib
+    m, keep = _fake_model(L)
+    x, y, kc, vc, ws = (ctypes.c_void_p(v) for v in (4096, 8192, 12288, 16384, 1 << 20))
+    need = lib.tfx_forward_kv_workspace_bytes(ctypes.byref(m), 2, 3)
+    # the KV path is always the per-op chain: the chain's workspace for 2 x 3 rows
+    per_row = 2 * 128 + 2 * 384 + 2 * 128 + 4 * 128 + 2 * 128
+    assert need == 6 * per_row
+    call = lambda **kw: lib.tfx_forward_kv(  # noqa: E731
+        ctypes.byref(kw.get("model", m)), kw.get("x", x), kw.get("y", y), kw.get("batch", 2),
+        kw.get("new", 3), kw.get("start", 5), kw.get("cap", 8), kw.get("kc", kc),
+        kw.get("vc", vc), kw.get("ws", ws), kw.get("ws_bytes", need), None)
+    assert call(start=6) == L.TFX_ERR_INVALID_ARGUMENT  # 6 + 3 > 8
+    assert b"capacity exceeded" in lib.tfx_last_error_message()
+    assert call(start=-1) == L.TFX_ERR_INVALID_ARGUMENT
+    assert call(new=0) == L.TFX_ERR_INVALID_ARGUMENT
+    assert call(kc=None) == L.TFX_ERR_INVALID_ARGUMENT
+    assert call(vc=ctypes.c_void_p(16386)) == L.TFX_ERR_MISALIGNED
+    assert call(ws=ctypes.c_void_p((1 << 20) + 16)) == L.TFX_ERR_MISALIGNED
+    assert call(ws_bytes=need - 1) == L.TFX_ERR_WORKSPACE
+    assert call(y=x) == L.TFX_ERR_INVALID_ARGUMENT
+    nc, keep2 = _fake_model(L, causal=0)
+    assert call(model=nc) == L.TFX_ERR_UNSUPPORTED
+    assert b"causal" in lib.tfx_last_error_message()
+    assert lib.tfx_forward_kv_workspace_bytes(ctypes.byref(m), 0, 3) == -1

@@ -114,8 +114,30 @@ def test_toggles_keep_reference_contract(pkg):
     m.enable_attention_fp16_accumulation(False)
     m.enable_triton_fused_norm(True)
     m.enable_triton_fused_ffn(True)
-    with pytest.raises(NotImplementedError):
+
+
+def test_kv_cache_contract(pkg):
+    """torch_transformer_benchmark.py:409-424, 1000-1003: causal models only,
+    eval mode only, reset clears the length, CPU inputs are refused."""
+    cfg = pkg.TransformerConfig(1, 8, 128, 4, 128, 1, False)
+    with pytest.raises(ValueError, match="causal"):
+        pkg.UserOptimizedTransformer(cfg).enable_kv_cache(True)
+    m = pkg.UserOptimizedTransformer(pkg.TransformerConfig(1, 8, 128, 4, 128, 1, True))
+    with pytest.raises(RuntimeError, match="eval"):
         m.enable_kv_cache(True)
+    m.eval()
+    m.enable_kv_cache(True)
+    assert m.kv_cache_length == 0
+    with pytest.raises(RuntimeError, match="CUDA inference"):
+        m(torch.zeros(1, 2, 128))
+    m._kv_cache_length = 3  # as after a decoded chunk
+    with pytest.raises(RuntimeError, match="reset the KV cache"):
+        m.enable_mixed_precision(torch.float16)
+    m.reset_kv_cache()
+    assert m.kv_cache_length == 0
+    m.enable_mixed_precision(torch.float16)
+    m.enable_kv_cache(False)
+    assert not m._kv_cache_enabled
 
 
 def test_ops_reject_cpu_tensors(pkg):
