@@ -82,6 +82,9 @@ def parse_args():
                     help="override the sequence length (small cases for ncu captures only)")
     ap.add_argument("--chain", action="store_true",
                     help="force the per-op kernel chain instead of the fused kernel")
+    ap.add_argument("--decode", type=int, default=None, metavar="CACHE_LEN",
+                    help="time KV-cached decoding instead: one new token per sequence over a "
+                         "cache of CACHE_LEN tokens (the config's geometry)")
     return ap.parse_args()
 
 
@@ -367,10 +370,111 @@ def algorithmic(kind, M, S, D, H, F):
     return table[kind]
 
 
+def run_decode(args):
+    """KV-cached decoding (the reference's enable_kv_cache path): each step
+    runs every layer for one new token per sequence, whose attention reads
+    the whole cache of `args.decode` earlier tokens. The cache holds
+    synthetic N(0,1) fp16 keys/values (their values do not change the work);
+    steps are CUDA Graph replays of tfx_forward_kv at a fixed cache length."""
+    import torch
+
+    pkg = importlib.import_module("gpu-kernel-for-transformer_b200")
+    lib = pkg._lib.load()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B, _, D, H, F, L = CONFIGS[args.config]
+    if args.batch:
+        B = args.batch
+    n = args.decode
+    cap = n + 1
+    torch.manual_seed(SEED)
+    model = pkg.UserOptimizedTransformer(pkg.TransformerConfig(B, cap, D, H, F, L, True))
+    model = model.to(dev).eval()
+    mdl = model._prepare(dev)[3]
+    g = torch.Generator(device=dev).manual_seed(SEED)
+    kc = torch.randn(L, B, cap, D, device=dev, dtype=torch.float16, generator=g)
+    vc = torch.randn(L, B, cap, D, device=dev, dtype=torch.float16, generator=g)
+    x = torch.randn(B, 1, D, device=dev, generator=g)
+    y = torch.empty_like(x)
+    ws = torch.empty(max(256, lib.tfx_forward_kv_workspace_bytes(ctypes.byref(mdl), B, 1)),
+                     dtype=torch.uint8, device=dev)
+
+    def step():
+        st = torch.cuda.current_stream().cuda_stream
+        pkg._lib.check(lib.tfx_forward_kv(ctypes.byref(mdl), x.data_ptr(), y.data_ptr(), B, 1, n,
+                                          cap, kc.data_ptr(), vc.data_ptr(), ws.data_ptr(),
+                                          ws.numel(), st), "tfx_forward_kv")
+
+    with torch.inference_mode():
+        for _ in range(3):
+            step()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        for _ in range(max(3, args.warmup)):
+            graph.replay()
+        sampler = ClockSampler(smi_gpu_id(0))
+        sampler.start()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        clocks = sampler.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    hbm, _, _, peak_kind = load_peaks()
+    # Compulsory bytes per step: every layer's K and V cache rows (n + 1
+    # keys, fp16) read once, the new K/V rows written, the weights read once,
+    # the token's fp32 input/output.
+    cache_bytes = 2 * L * B * (n + 1) * D * 2
+    weight_bytes = L * (4 * D * D + 2 * D * F) * 2
+    nbytes = cache_bytes + 2 * L * B * D * 2 + weight_bytes + B * D * 8
+    achieved = nbytes / (ms / 1e3) / 1e9
+    line = {
+        "metric": "decode tokens/sec (device-timed, KV cache)",
+        "value": B / (ms / 1e3),
+        "unit": UNIT,
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp16",
+        "data": "synthetic",
+        "config": {
+            "workload": f"{args.config} geometry: B={B}, D={D}, H={H}, F={F}, L={L}; one new "
+                        f"token per sequence over a {n}-token KV cache",
+            "global_batch": B, "kv_cache_tokens": n, "parallelism": "single GPU",
+            "l2": f"KV cache {cache_bytes / 1e9:.1f} GB per step, larger than L2; no flush",
+        },
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm, "traffic": None,
+                     "kernel": "decode step (all kernels; cache reads dominate)",
+                     "algorithmic_bytes_per_launch": nbytes, "mean_launch_ms": ms,
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"},
+        "cpu_baseline": None,
+        "cpu_baseline_note": "the reference's KV cache runs on CUDA only "
+                             "(torch_transformer_benchmark.py:1000-1002)",
+        "e2e": None,
+        "gpu_launches": args.steps * (1 + 8 * L),
+        "clocks": clocks,
+    }
+    print(json.dumps(line))
+    return 0
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.decode is not None:
+        return run_decode(args)
 
     import torch
     import torch.distributed as dist

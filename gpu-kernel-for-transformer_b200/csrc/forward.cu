@@ -74,6 +74,7 @@ struct Workspace {
   __half* ctx;
   float* res;
   __half* g;
+  float* part;  // KV decode steps only: split-KV attention partials
   size_t bytes;
 };
 
@@ -83,7 +84,8 @@ struct Workspace {
 // it is used with, where the transpose would cost more than it saves.)
 bool attention_reads_vt(int hd) { return hd == 64 || hd == 128; }
 
-Workspace plan_workspace(char* base, int batch, int seq, int d, int f, int hd) {
+Workspace plan_workspace(char* base, int batch, int seq, int d, int f, int hd,
+                         bool decode_scratch = false) {
   Workspace w{};
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -102,6 +104,8 @@ Workspace plan_workspace(char* base, int batch, int seq, int d, int f, int hd) {
   w.ctx = reinterpret_cast<__half*>(take(sizeof(__half) * m * d));
   w.res = reinterpret_cast<float*>(take(sizeof(float) * m * d));
   w.g = reinterpret_cast<__half*>(take(sizeof(__half) * m * f));
+  if (decode_scratch)
+    w.part = reinterpret_cast<float*>(take(attention_decode_part_bytes(batch, d / hd, seq, hd)));
   w.bytes = off;
   return w;
 }
@@ -173,8 +177,13 @@ int run_chain(const tfx_model* model, const float* x, float* y, int batch, int s
     if (kv != nullptr && kv->cache_len > 0) {
       const AttnKv geom{d, kv->capacity, kv->cache_len + seq, kv->cache_len};
       const size_t layer_elems = static_cast<size_t>(batch) * kv->capacity * d;
-      st = launch_attention_kv(ws.qkv, 3 * d, kv->k + l * layer_elems, kv->v + l * layer_elems,
-                               geom, ws.ctx, d, batch, nh, seq, hd, scale, stream);
+      if (seq <= kDecodeMaxQueries)  // decode step: split-KV over the cache
+        st = launch_attention_decode(ws.qkv, 3 * d, kv->k + l * layer_elems,
+                                     kv->v + l * layer_elems, geom, ws.ctx, d, batch, nh, seq, hd,
+                                     scale, ws.part, stream);
+      else
+        st = launch_attention_kv(ws.qkv, 3 * d, kv->k + l * layer_elems, kv->v + l * layer_elems,
+                                 geom, ws.ctx, d, batch, nh, seq, hd, scale, stream);
     } else if (attention_reads_vt(hd)) {
       st = launch_transpose_v(ws.qkv + 2 * d, 3 * d, ws.h, batch, seq, d, stream);
       if (st != TFX_OK) return st;
@@ -269,7 +278,8 @@ int tfx_forward(const tfx_model* model, const float* x, float* y, int batch, int
 int64_t tfx_forward_kv_workspace_bytes(const tfx_model* model, int batch, int new_tokens) {
   if (check_model(model) != TFX_OK || batch <= 0 || new_tokens <= 0) return -1;
   return static_cast<int64_t>(plan_workspace(nullptr, batch, new_tokens, model->d_model,
-                                            model->ffn_dim, model->d_model / model->num_heads)
+                                            model->ffn_dim, model->d_model / model->num_heads,
+                                            new_tokens <= kDecodeMaxQueries)
                                  .bytes);
 }
 
@@ -296,7 +306,8 @@ int tfx_forward_kv(const tfx_model* model, const float* x, float* y, int batch, 
     return fail(TFX_ERR_MISALIGNED,
                 "tfx_forward_kv: x/y/caches 16-byte and workspace 256-byte alignment");
   const int d = model->d_model, f = model->ffn_dim, hd = d / model->num_heads;
-  const Workspace ws = plan_workspace(static_cast<char*>(workspace), batch, new_tokens, d, f, hd);
+  const Workspace ws = plan_workspace(static_cast<char*>(workspace), batch, new_tokens, d, f, hd,
+                                      new_tokens <= kDecodeMaxQueries);
   if (workspace_bytes < ws.bytes)
     return fail(TFX_ERR_WORKSPACE, "tfx_forward_kv: workspace %zu < required %zu bytes",
                 workspace_bytes, ws.bytes);

@@ -90,6 +90,16 @@ struct AttnKv {
   int q_off;           // key position of query row 0 (causal: row i sees keys <= q_off + i)
 };
 
+// Decode steps (q_len <= kDecodeMaxQueries new queries per sequence over a KV
+// cache): split-KV kernel + combine; `part` is scratch of
+// attention_decode_part_bytes(batch, heads, q_len, head_dim) bytes.
+constexpr int kDecodeMaxQueries = 16;
+size_t attention_decode_part_bytes(int batch, int heads, int q_len, int head_dim);
+int launch_attention_decode(const __half* q, int64_t ld_q, const __half* k, const __half* v,
+                            const AttnKv& kv, __half* out, int64_t ld_out, int batch, int heads,
+                            int q_len, int head_dim, float scale, float* part,
+                            cudaStream_t stream);
+
 // Causal attention of q_len new queries per sequence (row pitch ld_q,
 // sequences q_len rows apart) over kv.len cached keys; every head_dim.
 int launch_attention_kv(const __half* q, int64_t ld_q, const __half* k, const __half* v,

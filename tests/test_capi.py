@@ -177,9 +177,14 @@ def test_kv_forward_validates_on_the_host(lib):
     m, keep = _fake_model(L)
     x, y, kc, vc, ws = (ctypes.c_void_p(v) for v in (4096, 8192, 12288, 16384, 1 << 20))
     need = lib.tfx_forward_kv_workspace_bytes(ctypes.byref(m), 2, 3)
-    # the KV path is always the per-op chain: the chain's workspace for 2 x 3 rows
+    # the KV path is always the per-op chain: the chain's workspace for 2 x 3 rows, plus
+    # (new_tokens <= 16: decode steps) split-KV partials for up to 4096 (batch, head,
+    # split) rows: fp32 O [rows][3][head_dim 32] and (max, sum) pairs
     per_row = 2 * 128 + 2 * 384 + 2 * 128 + 4 * 128 + 2 * 128
-    assert need == 6 * per_row
+    part = 4096 * 3 * 32 * 4 + 4096 * 3 * 8
+    assert need == 6 * per_row + (part + 255) // 256 * 256
+    big = lib.tfx_forward_kv_workspace_bytes(ctypes.byref(m), 2, 17)  # no decode scratch
+    assert big == 34 * per_row
     call = lambda **kw: lib.tfx_forward_kv(  # noqa: E731
         ctypes.byref(kw.get("model", m)), kw.get("x", x), kw.get("y", y), kw.get("batch", 2),
         kw.get("new", 3), kw.get("start", 5), kw.get("cap", 8), kw.get("kc", kc),
