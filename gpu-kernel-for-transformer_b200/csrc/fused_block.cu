@@ -799,7 +799,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int col = 64 * half + 32 * c;
             add_bias32(v[c], lp + kPIn + col);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[c][j] = gelu_as(v[c][j]);
+            for (int j = 0; j < 32; j += 2)
+              f2_unpack(gelu_poly_f2(f2_pack(v[c][j], v[c][j + 1])), v[c][j], v[c][j + 1]);
           }
           store_a_tmem(tl, half, v);
         }

@@ -239,7 +239,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                             v1.x + b1.x, v1.y + b1.y, v1.z + b1.z, v1.w + b1.w};
               if constexpr (EPI == TFX_EPI_BIAS_GELU) {
 #pragma unroll
-                for (int u = 0; u < 8; ++u) e[u] = gelu_as(e[u]);
+                for (int u = 0; u < 8; u += 2)
+                  f2_unpack(gelu_poly_f2(f2_pack(e[u], e[u + 1])), e[u], e[u + 1]);
               }
               *reinterpret_cast<uint4*>(static_cast<__half*>(out) + row * ldo + n0 + c + c8) =
                   make_uint4(pack_half2(e[0], e[1]), pack_half2(e[2], e[3]),

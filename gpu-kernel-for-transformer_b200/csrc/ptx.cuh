@@ -353,33 +353,6 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
-// 1/x with the hardware approximation (rcp.approx.ftz.f32).
-__device__ __forceinline__ float fast_rcp(float x) {
-  float y;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-// GELU in its exact form x * Phi(x), Phi(x) = (1 + erf(x / sqrt 2)) / 2, with
-// erf from Abramowitz & Stegun, Handbook of Mathematical Functions, 7.1.26:
-//   erf(z) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-z^2),
-//   t = 1 / (1 + p z), z >= 0, |error| <= 1.5e-7,
-// p = 0.3275911, a1..a5 = 0.254829592, -0.284496736, 1.421413741,
-// -1.453152027, 1.061405429. For x < 0 the tail term is used directly
-// (Phi(x) = (1 - erf(|z|)) / 2), so there is no cancellation. Branch-free;
-// |Phi error| <= 7.5e-8, far below the fp16 rounding of the result.
-__device__ __forceinline__ float gelu_as(float x) {
-  const float z = fabsf(x) * 0.70710678118654752f;
-  const float t = fast_rcp(fmaf(0.3275911f, z, 1.0f));
-  float poly = fmaf(1.061405429f, t, -1.453152027f);
-  poly = fmaf(poly, t, 1.421413741f);
-  poly = fmaf(poly, t, -0.284496736f);
-  poly = fmaf(poly, t, 0.254829592f);
-  poly *= t;
-  const float half_tail = 0.5f * poly * fast_exp2(-1.4426950408889634f * z * z);
-  return x * (x >= 0.f ? 1.0f - half_tail : half_tail);
-}
-
 // ------------------------------------------------- packed fp32 pairs (sm_100)
 // Two fp32 values in one 64-bit register pair; add/sub/fma.rn.f32x2 do both
 // lanes in one instruction (half the issue slots of scalar FADD/FFMA).
@@ -405,6 +378,40 @@ __device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
   uint64_t r;
   asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
   return r;
+}
+
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
+// Exact-erf GELU of a pair, x * Phi(x) = x/2 * (1 + erf(x / sqrt 2)), on the
+// FMA pipe only (no MUFU). erf(z) = zc * Q(t): zc = z clamped to [-3.5, 3.5]
+// (1 - erf(3.5) = 7.4e-7) and t = zc^2 * 2/3.5^2 - 1 in [-1, 1], where the
+// monomial basis is well conditioned for fp32. Q (degree 11) is a fit
+// computed for this file: Lawson's iteratively reweighted least squares
+// towards the minimax absolute error of erf on [0, 3.5]. Evaluated in fp32:
+// |erf error| <= 2e-6, |GELU error| <= 1e-5 (the fp16 the result is stored in
+// rounds by 2.4e-4 relative).
+__device__ __forceinline__ uint64_t gelu_poly_f2(uint64_t x) {
+  const uint64_t z = f2_mul(x, f2_pack(0.70710678118654752f, 0.70710678118654752f));
+  float z0, z1;
+  f2_unpack(z, z0, z1);
+  const uint64_t zc = f2_pack(fminf(fmaxf(z0, -3.5f), 3.5f), fminf(fmaxf(z1, -3.5f), 3.5f));
+  const uint64_t t = f2_fma(zc, f2_mul(zc, f2_pack(0.16326530277729034f, 0.16326530277729034f)),
+                            f2_pack(-1.0f, -1.0f));
+  constexpr float kQ[12] = {0.403872549533844f,     -0.20070447027683258f,
+                            0.1467849612236023f,    -0.1145324558019638f,
+                            0.08795613795518875f,   -0.06528491526842117f,
+                            0.04709062725305557f,   -0.028708625584840775f,
+                            0.01271552499383688f,   -0.008698718622326851f,
+                            0.008621933870017529f,  -0.0033988277427852154f};
+  uint64_t p = f2_pack(kQ[11], kQ[11]);
+#pragma unroll
+  for (int k = 10; k >= 0; --k) p = f2_fma(p, t, f2_pack(kQ[k], kQ[k]));
+  const uint64_t h = f2_mul(x, f2_pack(0.5f, 0.5f));
+  return f2_fma(h, f2_mul(zc, p), h);
 }
 
 // max(a, b, c) in one instruction (sm_100 three-input max).
