@@ -83,7 +83,7 @@ def parse_args():
     ap.add_argument("--chain", action="store_true",
                     help="force the per-op kernel chain instead of the fused kernel")
     ap.add_argument("--e2e-chunks", type=int, default=None,
-                    help="sub-batches per e2e step (default: ~160 MB host transfers, at most 8)")
+                    help="sub-batches per e2e step (default: host transfers of 128-256 MB, at most 8)")
     ap.add_argument("--decode", type=int, default=None, metavar="CACHE_LEN",
                     help="time KV-cached decoding instead: one new token per sequence over a "
                          "cache of CACHE_LEN tokens (the config's geometry)")
@@ -551,7 +551,7 @@ def main():
     # package's StreamingForward overlaps the download of one sub-batch, the
     # forward of the next and the upload of the one after on three streams
     # (PCIe is full duplex). A step's B sequences go through as `chunks`
-    # sub-batches of ~160 MB (sequences are independent), so the pipeline's
+    # sub-batches of 128-256 MB (sequences are independent), so the pipeline's
     # fill and drain are a fraction of a step (c2: 4 sub-batches 91.9 -> 94.8 M
     # tokens/s; pinned copies on the box run 50 GB/s per direction in duplex,
     # a 13.1 ms floor per step). The timed region spans the first upload to the
@@ -561,7 +561,7 @@ def main():
         x_pin = x_host.pin_memory()
         y_pin = torch.empty_like(x_pin).pin_memory()
         e2e_steps = max(3, min(args.steps, 20))
-        chunks = args.e2e_chunks or max(1, min(8, x_pin.numel() * 4 // (160 << 20)))
+        chunks = args.e2e_chunks or max(1, min(8, x_pin.numel() * 4 // (128 << 20)))
         while B % chunks:
             chunks -= 1
         bc = B // chunks
