@@ -616,11 +616,17 @@ def main():
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"}
     else:
         achieved = nflops / (mean_ms / 1e3) / 1e12
-        roof = {"bound": "tensor", "achieved": achieved, "peak": tf_burst, "unit": "TFLOP/s",
-                "frac": achieved / tf_burst, "traffic": traffic, "kernel": dom,
+        # Burst peak for a kernel that runs at full clock; the sustained
+        # (power-capped) peak when the GPU hit its power cap while this
+        # workload was timed (long tensor-bound steps such as c5's).
+        capped = bool(clocks) and "sw_power_cap" in (clocks.get("reasons") or []) and tf_sust
+        tf = tf_sust if capped else tf_burst
+        roof = {"bound": "tensor", "achieved": achieved, "peak": tf, "unit": "TFLOP/s",
+                "frac": achieved / tf, "traffic": traffic, "kernel": dom,
                 "algorithmic_flops_per_launch": nflops, "algorithmic_bytes_per_launch": nbytes,
                 "mean_launch_ms": mean_ms,
-                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json bf16_tflops)"}
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json "
+                               f"{'bf16_tflops_sustained: sw_power_cap active' if capped else 'bf16_tflops'})"}
 
     # ---- final gather of outputs to rank 0 (outside the timed region)
     gather_ms = None
