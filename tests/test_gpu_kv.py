@@ -37,6 +37,12 @@ KV_CASES = [
     (3, 200, 256, 2, 256, 1, [64, 1, 70, 2]),           # hd 128
     (1, 160, 512, 2, 512, 1, [40, 1, 1, 90]),           # hd 256
     (1, 260, 128, 4, 128, 1, [1] + [1] * 6 + [250]),    # decode from one token, then a long chunk
+    # 16 new tokens: the last split-KV decode step; 17: the offset path. Long
+    # caches with few (batch, head) pairs split the keys over several CTAs.
+    (1, 2100, 128, 2, 128, 1, [2000, 1, 16, 17, 1]),     # hd 64, up to 8 splits
+    (2, 700, 128, 4, 128, 1, [600, 16, 3, 17, 2]),       # hd 32
+    (1, 1100, 512, 2, 512, 1, [1000, 1, 5, 16]),         # hd 256, several splits
+    (1, 600, 128, 16, 128, 1, [520, 1, 16, 9]),          # hd 8
 ]
 
 
