@@ -24,7 +24,11 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;  // 64 fp16 = one 128-byte swizzle row
-constexpr int kThreads = 192;
+// Epilogue warps: two per TMEM lane quarter (SM sub-partition), each taking
+// half of a tile's columns. One warp per sub-partition was latency-bound:
+// a 128x256 tile's epilogue took ~10 us against ~5.4 us of MMAs.
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 
 template <int BN, int STAGES>
 struct GemmLayout {
@@ -32,11 +36,14 @@ struct GemmLayout {
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kBarOffset = STAGES * kStageBytes;
-  // Epilogue staging: per epilogue warp 32 rows x 32 fp32 columns, rows
-  // padded to 36 floats (16-byte aligned, conflict-free both ways).
-  static constexpr int kStgStride = 36;
+  // Epilogue staging: per epilogue warp 32 rows x 32 fp32 columns; the eight
+  // 16-byte chunks of row r sit at chunk index j ^ (r & 7), so the lane-per-row
+  // writes and the row-contiguous reads are both conflict-free.
+  static constexpr int kStgStride = 32;
   static constexpr int kStgOffset = kBarOffset + 256;
-  static constexpr int kStgBytes = 4 * 32 * kStgStride * 4;
+  static constexpr int kStgBytes = kEpiWarps * 32 * kStgStride * 4;
+  // Columns of a tile per epilogue warp (BN 32: one warp of each pair idles).
+  static constexpr int kEpiCols = BN >= 64 ? BN / 2 : BN;
   static constexpr int kSmemBytes = kStgOffset + kStgBytes + 1024;  // + 1 KB alignment slack
   static_assert(kSmemBytes <= 227 * 1024, "shared-memory budget");
   // Two accumulator buffers; TMEM allocations are powers of two >= 32 columns.
@@ -74,7 +81,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 128);
+      mbar_init(&acc_empty[b], 32 * kEpiWarps);
     }
     fence_mbar_init();
   }
@@ -160,6 +167,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp >= 2) {
     // ----------------------------------------------------------- epilogue
     const int quarter = warp & 3;
+    // This warp's columns of every tile: [cbeg, cend). (BN 32: the second
+    // warp of each pair has none; it still waits and arrives with the others
+    // so the accumulator barriers keep their counts.)
+    const int cbeg = ((warp - 2) >> 2) * L::kEpiCols;
+    const int cend = cbeg + L::kEpiCols <= BN ? cbeg + L::kEpiCols : cbeg;
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int buf = local & 1;
@@ -188,28 +200,29 @@ __global__ void __launch_bounds__(kThreads, 1)
                            : make_float4(0.f, 0.f, 0.f, 0.f);
         }
       };
-      if constexpr (EPI == TFX_EPI_BIAS_RESIDUAL) load_res(nxt, 0);
+      if (EPI == TFX_EPI_BIAS_RESIDUAL && cbeg < cend) load_res(nxt, cbeg);
       // The next chunk's TMEM load is in flight while this chunk is stored.
       uint32_t r[32];
-      tmem_ld32(t_row, r);
+      if (cbeg < cend) tmem_ld32(t_row + cbeg, r);
       const int sub = lane >> 2, c8 = (lane & 3) * 8;  // fp16 out: 4 lanes per row, 8 rows/pass
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
+      for (int c = cbeg; c < cend; c += 32) {
         if constexpr (EPI == TFX_EPI_BIAS_RESIDUAL) {
           // This chunk's residual was loaded one chunk ahead; start the next.
 #pragma unroll
           for (int i = 0; i < 8; ++i) res[i] = nxt[i];
-          if (c + 32 < BN) load_res(nxt, c + 32);
+          if (c + 32 < cend) load_res(nxt, c + 32);
         }
         tmem_ld_wait();
         // Lane = row: the raw accumulator into the staging tile.
         float4* srow = reinterpret_cast<float4*>(stg + lane * L::kStgStride);
 #pragma unroll
         for (int j = 0; j < 8; ++j)
-          srow[j] = make_float4(__uint_as_float(r[4 * j + 0]), __uint_as_float(r[4 * j + 1]),
-                                __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+          srow[j ^ (lane & 7)] =
+              make_float4(__uint_as_float(r[4 * j + 0]), __uint_as_float(r[4 * j + 1]),
+                          __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
         __syncwarp();
-        if (c + 32 < BN) tmem_ld32(t_row + c + 32, r);
+        if (c + 32 < cend) tmem_ld32(t_row + c + 32, r);
         // Row-contiguous phase: consecutive lanes take consecutive columns, so
         // each lane needs only its own columns' bias.
         if constexpr (EPI == TFX_EPI_BIAS_RESIDUAL) {
@@ -219,7 +232,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int rr = rsub + 4 * i;
             const int row = wrow0 + rr;
             if (row < M) {
-              const float4 v = *reinterpret_cast<const float4*>(stg + rr * L::kStgStride + rc4);
+              const float4 v = reinterpret_cast<const float4*>(
+                  stg + rr * L::kStgStride)[(rc4 >> 2) ^ (rr & 7)];
               *reinterpret_cast<float4*>(static_cast<float*>(out) + row * ldo + n0 + c + rc4) =
                   make_float4((v.x + bb.x) + res[i].x, (v.y + bb.y) + res[i].y,
                               (v.z + bb.z) + res[i].z, (v.w + bb.w) + res[i].w);
@@ -232,9 +246,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int rr = sub; rr < 32; rr += 8) {
             const int row = wrow0 + rr;
             if (row < M) {
-              const float4 v0 = *reinterpret_cast<const float4*>(stg + rr * L::kStgStride + c8);
-              const float4 v1 =
-                  *reinterpret_cast<const float4*>(stg + rr * L::kStgStride + c8 + 4);
+              const float4* sr = reinterpret_cast<const float4*>(stg + rr * L::kStgStride);
+              const float4 v0 = sr[(c8 >> 2) ^ (rr & 7)];
+              const float4 v1 = sr[((c8 >> 2) + 1) ^ (rr & 7)];
               float e[8] = {v0.x + b0.x, v0.y + b0.y, v0.z + b0.z, v0.w + b0.w,
                             v1.x + b1.x, v1.y + b1.y, v1.z + b1.z, v1.w + b1.w};
               if constexpr (EPI == TFX_EPI_BIAS_GELU) {
@@ -306,7 +320,7 @@ int launch_gemm_epi(const __half* a, int64_t lda, const __half* w, const float* 
   if (s256 > 0 && s256 >= s192 && s256 >= s128)
     return launch_gemm_t<256, 4, EPI>(a, lda, w, bias, residual, ldr, out, ldo, m, n, k, stream);
   if (s192 > 0 && s192 >= s128)
-    return launch_gemm_t<192, 5, EPI>(a, lda, w, bias, residual, ldr, out, ldo, m, n, k, stream);
+    return launch_gemm_t<192, 4, EPI>(a, lda, w, bias, residual, ldr, out, ldo, m, n, k, stream);
   if (n % 128 == 0)
     return launch_gemm_t<128, 6, EPI>(a, lda, w, bias, residual, ldr, out, ldo, m, n, k, stream);
   if (n % 64 == 0)
