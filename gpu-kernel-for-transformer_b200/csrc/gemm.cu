@@ -304,10 +304,12 @@ template <int EPI>
 int launch_gemm_epi(const __half* a, int64_t lda, const __half* w, const float* bias,
                     const float* residual, int64_t ldr, void* out, int64_t ldo, int64_t m, int n,
                     int k, cudaStream_t stream) {
-  // N tile: wide tiles mean fewer A re-reads, but the tile count should also
-  // fill the last wave of the persistent grid (768 tiles of 256 on 148 SMs
-  // are 5.19 waves; 1024 tiles of 192 are 6.92). Score = wave efficiency,
-  // discounted for the narrower tile's extra operand traffic.
+  // N tile: the tile count should fill the last wave of the persistent grid
+  // (768 tiles of 256 on 148 SMs are 5.19 waves; 1024 tiles of 192 are 6.92),
+  // but narrow tiles cost more per output: the mainloop is bound by shared-
+  // memory bandwidth (TMA writes plus tensor-core operand reads), so a
+  // 128x256 tile takes ~190 cycles per K=16 step (the measured cuBLAS rate)
+  // and a 128x192 tile ~183. Score = wave efficiency x relative throughput.
   const int sms = num_sms();
   const int64_t mt = (m + kBM - 1) / kBM;
   auto score = [&](int bn, double per_tile) {
@@ -316,7 +318,7 @@ int launch_gemm_epi(const __half* a, int64_t lda, const __half* w, const float* 
     const int64_t waves = (t + sms - 1) / sms;
     return per_tile * static_cast<double>(t) / static_cast<double>(waves * sms);
   };
-  const double s256 = score(256, 1.0), s192 = score(192, 0.97), s128 = score(128, 0.92);
+  const double s256 = score(256, 1.0), s192 = score(192, 0.78), s128 = score(128, 0.70);
   if (s256 > 0 && s256 >= s192 && s256 >= s128)
     return launch_gemm_t<256, 4, EPI>(a, lda, w, bias, residual, ldr, out, ldo, m, n, k, stream);
   if (s192 > 0 && s192 >= s128)

@@ -73,6 +73,12 @@ GEMM_SHAPES = [
     (77, 96, 40),
     (1, 32, 8),
     (40000, 128, 128),
+    # deep-K shapes with ragged M and each N-tile width
+    (300, 512, 512),
+    (1100, 384, 768),
+    (2048, 1024, 2048),
+    (512, 128, 1024),
+    (4096, 1024, 1024),
 ]
 
 
