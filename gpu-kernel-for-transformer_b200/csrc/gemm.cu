@@ -7,15 +7,16 @@
 // written by TMA. The fp32 accumulator lives in TMEM, double-buffered so the
 // epilogue of tile i overlaps the MMAs of tile i+1.
 //
-// CTA = 6 warps, one CTA per SM, grid = min(#tiles, #SMs):
+// CTA = 10 warps, one CTA per SM, grid = min(#tiles, #SMs):
 //   warp 0      TMA producer (one lane): A and W k-blocks into a STAGES ring
 //   warp 1      TMEM allocator + MMA issuer (one lane)
-//   warps 2..5  epilogue: tcgen05.ld rows out of TMEM, bias / GELU (exact
-//               erf form, Abramowitz & Stegun 7.1.26 erf), then
-//               through a per-warp shared-memory staging tile so that the
-//               residual loads and the output stores are coalesced (a lane
-//               per row would touch 32 rows per warp-wide access). Warp w
-//               may only touch TMEM lanes [32*(w%4), +32).
+//   warps 2..9  epilogue, two warps per TMEM lane quarter (warp w may only
+//               touch lanes [32*(w%4), +32)), each taking half of a tile's
+//               columns: tcgen05.ld rows out of TMEM, then through a per-warp
+//               shared-memory staging tile so that the bias / exact-erf GELU
+//               (gelu_poly_f2) / residual work, the residual loads and the
+//               output stores are row-contiguous and coalesced (a lane per
+//               row would touch 32 rows per warp-wide access).
 #include "internal.h"
 #include "ptx.cuh"
 
