@@ -95,3 +95,23 @@ class StreamingForward:
         done.record(self.down)
         caller.wait_stream(self.down)
         return done
+
+    def capture(self, x_host: Sequence[torch.Tensor], y_host: Sequence[torch.Tensor],
+                valid_len: Optional[torch.Tensor] = None) -> torch.cuda.CUDAGraph:
+        """The whole pipelined run(x_host, y_host) as one CUDA Graph, for a
+        serving loop that refills the same pinned host buffers: each replay
+        uploads every x_host[i], runs its forward and downloads into
+        y_host[i], with the same stream overlap as run(), and no per-step
+        host work. Replay on the caller's stream; read y_host after the
+        replay has completed.
+
+        The capture starts from fresh slots, so its waits refer only to events
+        recorded inside it; replays are ordered on the stream, so one replay's
+        slot reuse never races the next."""
+        torch.cuda.synchronize(self.device)
+        self._steps = 0
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            self.run(x_host, y_host, valid_len)
+        self._steps = 0
+        return graph
