@@ -235,3 +235,22 @@ def test_streaming_capture_replays_match_model(pkg, dev, cfg):
             torch.cuda.synchronize()
             for x, y in zip(xs, ys):
                 assert torch.equal(y, cand(x.to(dev)).cpu())
+
+
+@pytest.mark.parametrize("shape_id", list(range(1, 14)))
+def test_official_shapes_match_oracle(pkg, dev, shape_id):
+    """Every shape of the reference's official table (torch_transformer_benchmark.py:80-95)
+    except 14 (c5: the prefix test above) on the GPU, full batch, against the FP32
+    oracle on the first sequences (batch items are independent)."""
+    import dataclasses
+
+    cfg = dataclasses.asdict(pkg.OFFICIAL_BENCHMARK_SHAPES[shape_id])
+    oracle_model, cand = _pair(pkg, cfg, 1234, dev)
+    x, mask = ob.generate_random_case(ob.TransformerConfig(**cfg), 4321 + shape_id)
+    n = min(cfg["batch_size"], 64)
+    with torch.inference_mode():
+        y = cand(x.to(dev), mask.to(dev)).cpu()
+        ref = oracle_model(x[:n].contiguous(), mask[:n].contiguous())
+    res = ob.compare_outputs(ref, y[:n], RTOL, ATOL)
+    assert res.failed_elements == 0, (shape_id, res.failed_elements, res.max_abs_error)
+    assert bool(torch.isfinite(y).all())
