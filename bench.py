@@ -464,7 +464,9 @@ def run_decode(args):
         "cpu_baseline_note": "the reference's KV cache runs on CUDA only "
                              "(torch_transformer_benchmark.py:1000-1002)",
         "e2e": None,
-        "gpu_launches": args.steps * (1 + 8 * L),
+        # LayerNorm, then per layer QKV GEMM, KV append, split-KV decode
+        # attention + combine, out-proj, LayerNorm, FFN-in, FFN-out, LayerNorm.
+        "gpu_launches": args.steps * (1 + 9 * L),
         "clocks": clocks,
     }
     print(json.dumps(line))
