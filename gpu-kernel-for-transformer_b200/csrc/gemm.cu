@@ -69,8 +69,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // Tiles in N-fastest order: the CTAs running at once share a few A row
+  // blocks (read from DRAM once, then from L2) and all of W; M-fastest order
+  // streamed the whole of A once per N block (c5 QKV: 2.46 GB of DRAM reads
+  // for a 205 MB A).
   const int tiles_m = (M + kBM - 1) / kBM;
-  const int num_tiles = tiles_m * (N / BN);
+  const int tiles_n = N / BN;
+  const int num_tiles = tiles_m * tiles_n;
   const int kblocks = (K + kBK - 1) / kBK;
 
   if (threadIdx.x == 0) {
@@ -105,8 +110,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < STAGES; ++s) issued_parity[s] = -1;
     bool ok = true;
     for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-      const int m0 = (tile % tiles_m) * kBM;
-      const int n0 = (tile / tiles_m) * BN;
+      const int m0 = (tile / tiles_n) * kBM;
+      const int n0 = (tile % tiles_n) * BN;
       for (int kb = 0; kb < kblocks; ++kb) {
         if (!mbar_wait(&empty[stage], phase ^ 1, err, kDevTimeoutEmpty)) {
           ok = false;
@@ -181,8 +186,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[buf], use & 1, err, kDevTimeoutAccum)))
         break;
       tc_fence_after();
-      const int m0 = (tile % tiles_m) * kBM;
-      const int n0 = (tile / tiles_m) * BN;
+      const int m0 = (tile / tiles_n) * kBM;
+      const int n0 = (tile % tiles_n) * BN;
       const int wrow0 = m0 + quarter * 32;  // this warp's 32 rows
       const uint32_t t_row =
           tmem_base + static_cast<uint32_t>(buf * BN) + (static_cast<uint32_t>(quarter * 32) << 16);
