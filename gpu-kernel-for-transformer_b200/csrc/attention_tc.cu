@@ -94,7 +94,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v, __half* __restrict__ out,
                         int64_t ld_out, int heads, int q_len, int nqb, int kv_len, int q_off,
-                        float scale_log2, const int32_t* __restrict__ valid_len, int* err) {
+                        float scale_log2, const int32_t* __restrict__ valid_len, int bh_in_y,
+                        int* err) {
   grid_dep_wait();
   grid_dep_launch();
   using L = TcAttn<HD>;
@@ -118,10 +119,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int h = static_cast<int>(blockIdx.x % heads);
-  const int b = static_cast<int>(blockIdx.x / heads);
+  // bh_in_y: grid x = query block, y = batch * heads, so the CTAs running at
+  // once are mostly query blocks of one (b, h) and share its K/V in L2.
+  // Otherwise x = batch * heads (globally heaviest-first order).
+  const int bh = static_cast<int>(bh_in_y ? blockIdx.y : blockIdx.x);
+  const int qblk = static_cast<int>(bh_in_y ? blockIdx.x : blockIdx.y);
+  const int h = bh % heads;
+  const int b = bh / heads;
   // Causal: the heaviest query blocks (the last ones) are launched first.
-  const int qb = CAUSAL ? nqb - 1 - static_cast<int>(blockIdx.y) : static_cast<int>(blockIdx.y);
+  const int qb = CAUSAL ? nqb - 1 - qblk : qblk;
   const int q0 = qb * L::kNT * kTile;
   // Query row i of this sequence sits at key position q_off + i (q_off > 0:
   // new tokens attending a KV cache); causal rows see keys <= their position.
@@ -532,10 +538,18 @@ int launch_tc(const __half* q, int64_t ld_q, const __half* k, const __half* v, i
   }
   if (st != TFX_OK) return st;
   const int nqb = (q_len + L::kNT * kTile - 1) / (L::kNT * kTile);
-  const dim3 grid(static_cast<unsigned>(batch) * static_cast<unsigned>(heads),
-                  static_cast<unsigned>(nqb));
+  // Query blocks of one (b, h) side by side when all K/V is well beyond L2
+  // (long sequences): fewer DRAM reads lower the power draw, and under the
+  // power cap the SM clock rises (B=4, S=100k, hd 64: 1488 -> 1739 MHz,
+  // 122.6 -> 105.4 ms at equal cycles). Below that, (b, h)-fastest order keeps
+  // the global heaviest-first schedule (S=32k, B=1: 5.6 % faster).
+  const unsigned bh = static_cast<unsigned>(batch) * static_cast<unsigned>(heads);
+  const double kv_bytes = 4.0 * static_cast<double>(bh) * static_cast<double>(kv.len) * HD;
+  const int bh_in_y = (bh <= 65535u && nqb >= 4 && kv_bytes > 256.0 * (1 << 20)) ? 1 : 0;
+  const dim3 grid = bh_in_y ? dim3(static_cast<unsigned>(nqb), bh) : dim3(bh, static_cast<unsigned>(nqb));
   launch_pdl(kern, grid, dim3(kTcThreads), L::kSmem, stream, tq, tk, tv, out, ld_out, heads, q_len,
-             nqb, kv.len, kv.q_off, scale * 1.4426950408889634f, valid_len, device_error_word());
+             nqb, kv.len, kv.q_off, scale * 1.4426950408889634f, valid_len, bh_in_y,
+             device_error_word());
   return check_launch("attention_tc_kernel");
 }
 
