@@ -562,7 +562,7 @@ def main():
     if not args.no_e2e:
         x_pin = x_host.pin_memory()
         y_pin = torch.empty_like(x_pin).pin_memory()
-        e2e_steps = max(3, min(args.steps, 20))
+        e2e_steps = max(3, min(args.steps, 40))  # pipeline fill and drain: ~3 % of 20 steps
         chunks = args.e2e_chunks or max(1, min(8, x_pin.numel() * 4 // (128 << 20)))
         while B % chunks:
             chunks -= 1
