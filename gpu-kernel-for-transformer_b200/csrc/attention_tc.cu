@@ -1,4 +1,5 @@
-// Flash attention on the 5th-generation tensor cores, head_dim 64 and 128.
+// Flash attention on the 5th-generation tensor cores, head_dim 64, 128 and
+// 256 (256: one query tile per CTA, one K/V stage).
 //
 // CTA = 256 query rows of one (batch, head), split into two 128-row tiles A
 // and B that share every K/V tile; 11 warps, one CTA per SM:
@@ -38,9 +39,16 @@
 // Scores are handled in the log2 domain: c = scale * log2(e) folds the
 // softmax scale into the exponent's FMA.
 //
-// Masking: causal (key > query) and key padding (key >= valid_len[b]) apply
-// only on a tile's diagonal / ragged KV tile. Rows past the sequence end are
-// read as zeros by the 3-D tensor maps and never stored.
+// Masking: causal (key > query position) and key padding (key >=
+// valid_len[b]) apply only on a tile's diagonal / ragged KV tile. Rows past
+// the sequence end are read as zeros by the 3-D tensor maps and never stored.
+// Queries may sit at an offset among the keys (new tokens over a KV cache:
+// query row i at key position q_off + i).
+//
+// Grid: query blocks heaviest-first. When all K/V is well beyond L2, the
+// query blocks of one (batch, head) run side by side and share its K/V in L2
+// (fewer DRAM reads: under the power cap the SM clock rises); otherwise
+// (batch, head) varies fastest, for a globally heaviest-first schedule.
 //
 // Replaces the reference's attention call, F.scaled_dot_product_attention
 // with is_causal=True inside _fast_attention_impl
