@@ -51,7 +51,10 @@ class ForwardGraph:
         torch.cuda.current_stream(device).wait_stream(side)
         torch.cuda.synchronize(device)
         self.graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.graph):
+        # thread_local: only this thread's CUDA calls are checked during the
+        # capture, so another thread of the process (a NCCL process group's
+        # watchdog polling its events) cannot invalidate it.
+        with torch.cuda.graph(self.graph, capture_error_mode="thread_local"):
             model.run_into(x, y, valid_len, self.workspace)
         torch.cuda.synchronize(device)
 

@@ -111,7 +111,9 @@ class StreamingForward:
         torch.cuda.synchronize(self.device)
         self._steps = 0
         graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
+        # thread_local: other threads (a NCCL watchdog) stay free to query
+        # their events while this thread captures.
+        with torch.cuda.graph(graph, capture_error_mode="thread_local"):
             self.run(x_host, y_host, valid_len)
         self._steps = 0
         return graph
