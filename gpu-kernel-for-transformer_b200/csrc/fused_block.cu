@@ -11,7 +11,7 @@
 // TMA ring; biases and LayerNorm parameters sit in shared memory.
 //
 // Roles (320 threads):
-//   warp 0      TMA producer: per layer Wq, Wk, Wv, Wo, W1, W2 (128x128 fp16
+//   warp 0      TMA producer: per layer Wv, Wk, Wq, Wo, W1, W2 (128x128 fp16
 //               each, 128-byte swizzle) into a 3-slot ring
 //   warp 1      TMEM owner (all 512 columns) + single-thread tcgen05.mma issuer
 //   warps 2..9  compute, two warps per TMEM lane quarter: lane l of warp w
@@ -27,9 +27,10 @@
 //
 // Per layer (c = compute warps, m = MMA thread):
 //   c: LN1(x) -> sA (fp16, K-major, 128B swizzle)
-//   m: Q = h.Wq^T, K = h.Wk^T, V^T = Wv.h^T (V^T computed transposed so it is
-//      already the K-major B operand of P.V)
-//   c: + biases -> Q into sA, K into sK, V^T into sV
+//   m: V^T = Wv.h^T (computed transposed so it is already the K-major B
+//      operand of P.V), K = h.Wk^T, Q = h.Wq^T, each committed on its own
+//   c: + biases -> V^T into sV, K into sK (while the next GEMM runs), Q into
+//      sA last (over h, which all three GEMMs read)
 //   m: S_0 -> S buffer 0, S_1 -> S buffer 1
 //   per head h (b = h % 2):
 //     c: softmax row of S_h -> P_h (fp16, <= 1) written over its own S buffer
@@ -105,7 +106,7 @@ constexpr int kOffPar = kOffW + kWSlots * kOpBytes;
 constexpr int kOffXch = kOffPar + kParBytes;
 constexpr int kOffSum = kOffXch + kXchBytes;
 constexpr int kOffBar = kOffSum + kSumBytes;
-constexpr int kSmemBytes = kOffBar + 128 + 1024;
+constexpr int kSmemBytes = kOffBar + 192 + 1024;
 constexpr int kComputeWarps = 8;
 constexpr int kThreads = 32 * (2 + kComputeWarps);
 constexpr uint32_t kColS0 = 0;    // S buffer 0 (P_h aliased into it)
@@ -326,7 +327,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   // two S buffers in flight a lightly loaded warp may finish head h+1 before
   // a heavy warp finishes head h, so one barrier would let phases run ahead.
   uint64_t* c2m_p = m2c_o + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(c2m_p + 2);
+  uint64_t* m2c_v = c2m_p + 2;  // MMA -> compute: V^T accumulator ready
+  uint64_t* m2c_k = m2c_v + 1;  // MMA -> compute: K accumulator ready
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(m2c_k + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -341,6 +344,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&m2c_o[b], 1);
       mbar_init(&c2m_p[b], kComputeWarps);
     }
+    mbar_init(m2c_v, 1);
+    mbar_init(m2c_k, 1);
     fence_mbar_init();
   }
   grid_dep_wait();
@@ -385,11 +390,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < kWSlots; ++s) issued[s] = -1;
     bool ok = true;
     for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+      // The producer runs ahead of the compute warps (here: about one layer
+      // of the previous tile), so the tile's fp32 input is an L2 hit by the
+      // time they load it.
+      const int64_t row0 = static_cast<int64_t>(tile) * kT;
+      const int64_t nrows = p.rows - row0 < kT ? p.rows - row0 : kT;
+      bulk_prefetch_l2(p.x + row0 * kT, static_cast<uint32_t>(nrows * kT * 4));
       for (int l = 0; l < L && ok; ++l) {
         for (int c = 0; c < 6; ++c) {
           const CUtensorMap* m =
               c < 3 ? &p.w_qkv[l] : (c == 3 ? &p.w_out[l] : (c == 4 ? &p.w_in[l] : &p.w_fo[l]));
-          const int row0 = c < 3 ? kT * c : 0;
+          const int row0 = c < 3 ? kT * (2 - c) : 0;  // Wv, Wk, Wq
           if (!mbar_wait(&w_empty[slot], ph ^ 1, p.err, kDevTimeoutEmpty)) {
             ok = false;
             break;
@@ -458,14 +469,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int l = 0; l < L && ok; ++l) {
         uint64_t w;
         if (!(ok = wait_c2m())) break;  // LN1 output in sA
+        // V^T, K, Q, each with its own commit: the compute warps store V^T
+        // and K while the later GEMMs run; Q comes last because it is
+        // written over h in sA, which all three read.
         if (!(ok = take_w(w))) break;
-        mma_chain<kT / 16>(tmem + 0, dA, 0, w, 0, id128);  // Q
+        mma_chain<kT / 16>(tmem + 256, w, 0, dA, 0, id128);  // V^T = Wv . h^T
         release_w();
+        mma_commit(m2c_v);
         if (!(ok = take_w(w))) break;
         mma_chain<kT / 16>(tmem + 128, dA, 0, w, 0, id128);  // K
         release_w();
+        mma_commit(m2c_k);
         if (!(ok = take_w(w))) break;
-        mma_chain<kT / 16>(tmem + 256, w, 0, dA, 0, id128);  // V^T = Wv . h^T
+        mma_chain<kT / 16>(tmem + 0, dA, 0, w, 0, id128);  // Q
         release_w();
         mma_commit(m2c_g);
         if (!(ok = wait_c2m())) break;  // Q, K, V^T in smem
@@ -515,7 +531,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = q * 32 + lane;
     const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16);
     Pair pr{xch, half, r, 1 + q, 0};
-    uint32_t ph_g = 0, ph_s[2] = {0, 0}, ph_o[2] = {0, 0};
+    uint32_t ph_g = 0, ph_v = 0, ph_k = 0, ph_s[2] = {0, 0}, ph_o[2] = {0, 0};
     // Warp-uniform outcome: a timeout seen by one lane ends the whole warp.
     auto wait = [&](uint64_t* bar, uint32_t& phase) {
       const bool ok = __all_sync(0xffffffffu, mbar_wait(bar, phase, p.err, kDevTimeoutAccum));
@@ -614,43 +630,48 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int l = 0; l < L; ++l) {
         const float* lp = par + l * kParFloats;
         signal();  // LN1 output in sA
-        if (!(ok = wait(m2c_g, ph_g))) break;
-        // QKV epilogue: half 0 takes Q and the first half of the tokens of
-        // V^T row r; half 1 takes K and the second half. V^T lanes are features.
+        // QKV epilogue in the order the GEMMs complete: V^T (half 0 takes the
+        // first half of the tokens of V^T row r, half 1 the second; V^T lanes
+        // are features), then K (half 1), then Q (half 0).
+        if (!(ok = wait(m2c_v, ph_v))) break;
         {
           const float bv = lp[kPQkv + 256 + r];  // V bias of feature r
+          uint32_t ra[32], rb[32];
+          tmem_ld32(tl + 256 + 64 * half, ra);
+          tmem_ld32(tl + 256 + 64 * half + 32, rb);
+          tmem_ld_wait();
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(ra[j]) + bv;
+          store_row<4>(sV, r, 64 * half, v);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(rb[j]) + bv;
+          store_row<4>(sV, r, 64 * half + 32, v);
+        }
+        if (!(ok = wait(m2c_k, ph_k))) break;
+        if (half == 0 && !(ok = wait(m2c_g, ph_g))) break;
 #pragma unroll 1
-          for (int i = 0; i < 6; i += 2) {  // two chunks per TMEM wait
-            // i < 4: Q chunks 0..3 (half 0) or K chunks 4..7 (half 1);
-            // i >= 4: token chunks of V^T row r.
-            const uint32_t col0 = i < 4 ? 32 * (4 * half + i) : 256 + 32 * (2 * half + i - 4);
-            uint32_t ra[32], rb[32];
-            tmem_ld32(tl + col0, ra);
-            tmem_ld32(tl + col0 + 32, rb);
-            tmem_ld_wait();
-            float v[2][32];
+        for (int i = 0; i < 4; i += 2) {  // Q chunks 0..3 (half 0) or K chunks 4..7 (half 1)
+          uint32_t ra[32], rb[32];
+          tmem_ld32(tl + 32 * (4 * half + i), ra);
+          tmem_ld32(tl + 32 * (4 * half + i) + 32, rb);
+          tmem_ld_wait();
+          float v[2][32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              v[0][j] = __uint_as_float(ra[j]);
-              v[1][j] = __uint_as_float(rb[j]);
-            }
+          for (int j = 0; j < 32; ++j) {
+            v[0][j] = __uint_as_float(ra[j]);
+            v[1][j] = __uint_as_float(rb[j]);
+          }
 #pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              if (i < 4) {
-                const int c = 4 * half + i + u;
-                add_bias32(v[u], lp + kPQkv + 32 * c);
-                if (half == 0)
-                  store_q32<HD>(sA, r, 32 * (i + u), v[u]);
-                else
-                  store_row<4>(sK, r, 32 * (i + u), v[u]);
-              } else {
-#pragma unroll
-                for (int j = 0; j < 32; ++j) v[u][j] += bv;
-                store_row<4>(sV, r, 32 * (2 * half + i - 4 + u), v[u]);
-              }
-            }
+          for (int u = 0; u < 2; ++u) {
+            add_bias32(v[u], lp + kPQkv + 32 * (4 * half + i + u));
+            if (half == 0)
+              store_q32<HD>(sA, r, 32 * (i + u), v[u]);
+            else
+              store_row<4>(sK, r, 32 * (i + u), v[u]);
           }
         }
+        if (half == 1 && !(ok = wait(m2c_g, ph_g))) break;  // keeps this warp's m2c_g phase
         signal();
         // Attention, double-buffered over heads.
 #pragma unroll 1
@@ -670,8 +691,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             plain[c] = plain_tile && (!p.causal || ch < qq_e);
           }
           // Pass 1: masked row max. Both chunks come in with one TMEM round
-          // trip (pass 2 reloads them one at a time: keeping both live across
-          // the exchange would spill).
+          // trip and stay in registers across the exchange for pass 2.
           float mx = -INFINITY;
           uint32_t sr[2][32];
           tmem_ld32(sb + 64 * half, sr[0]);
@@ -703,21 +723,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           // All keys padding (zero-length sequence): weights exp2(-inf) = 0.
           const float mref = (mx == -INFINITY) ? 0.f : mx * sl2;
           // Pass 2: exp2, row sum, fp16 packing (f32x2 arithmetic on plain
-          // chunks).
+          // chunks), from the registers pass 1 loaded.
           float sum2[2] = {0.f, 0.f};
           uint64_t ls0 = 0, ls1 = 0;
           const uint64_t c2 = f2_pack(sl2, sl2), negm2 = f2_pack(-mref, -mref);
           uint32_t w[32];
-          uint32_t sr2[2][32];  // both chunks, one TMEM round trip
-          tmem_ld32(sb + 64 * half, sr2[0]);
-          tmem_ld32(sb + 64 * half + 32, sr2[1]);
-          tmem_ld_wait();
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             if (in[c]) {
               float sc[32];
 #pragma unroll
-              for (int j = 0; j < 32; ++j) sc[j] = __uint_as_float(sr2[c][j]);
+              for (int j = 0; j < 32; ++j) sc[j] = __uint_as_float(sr[c][j]);
               const int k0 = 32 * (2 * half + c);
               if (plain[c]) {
 #pragma unroll
