@@ -46,6 +46,10 @@
 // row 127-t (the QKV epilogue writes Q_h rows reversed; ctx_h is written back
 // in token order), so every sub-partition gets the same total over two heads.
 //
+// Every wait sleeps between polls (mbar_wait_sleep): the producer and MMA
+// warps share SM sub-partitions 0 and 1 with four compute warps and spend
+// most of their time waiting.
+//
 // tcgen05.ld/st are warp-collective: every TMEM access of the compute warps
 // is executed by all 32 lanes; rows past the end of the batch and padded
 // tokens are handled by predicating only the global stores.
@@ -401,7 +405,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const CUtensorMap* m =
               c < 3 ? &p.w_qkv[l] : (c == 3 ? &p.w_out[l] : (c == 4 ? &p.w_in[l] : &p.w_fo[l]));
           const int row0 = c < 3 ? kT * (2 - c) : 0;  // Wv, Wk, Wq
-          if (!mbar_wait(&w_empty[slot], ph ^ 1, p.err, kDevTimeoutEmpty)) {
+          if (!mbar_wait_sleep(&w_empty[slot], ph ^ 1, p.err, kDevTimeoutEmpty)) {
             ok = false;
             break;
           }
@@ -419,7 +423,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (!ok)  // unwinding after a timeout: let our own copies land first
       for (int s = 0; s < kWSlots; ++s)
-        if (issued[s] >= 0) mbar_wait(&w_full[s], issued[s], nullptr, 0);
+        if (issued[s] >= 0) mbar_wait_sleep(&w_full[s], issued[s], nullptr, 0);
   } else if (warp == 1 && lane == 0) {
     // ----------------------------------------------------------- MMA issuer
     constexpr uint32_t id128 = idesc_f16_f32(128, 128);
@@ -429,7 +433,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t mph_o[2] = {0, 0};  // this thread's view of the O-buffer barriers
     uint32_t mph_p[2] = {0, 0};  // ... and of the P-ready barriers
     auto wait_c2m = [&]() {
-      const bool r = mbar_wait(c2m, c2m_ph, p.err, kDevTimeoutOther);
+      const bool r = mbar_wait_sleep(c2m, c2m_ph, p.err, kDevTimeoutOther);
       c2m_ph ^= 1;
       tc_fence_after();
       return r;
@@ -437,7 +441,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint64_t dA = sdesc_k_sw128(sA), dK = sdesc_k_sw128(sK), dV = sdesc_k_sw128(sV);
     const uint64_t dW0 = sdesc_k_sw128(sbase + kOffW);
     auto take_w = [&](uint64_t& w) {
-      if (!mbar_wait(&w_full[slot], ph, p.err, kDevTimeoutFull)) return false;
+      if (!mbar_wait_sleep(&w_full[slot], ph, p.err, kDevTimeoutFull)) return false;
       tc_fence_after();
       w = dW0 + static_cast<uint64_t>(slot * (kOpBytes >> 4));
       return true;
@@ -489,7 +493,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (H > 1) issue_s(1);
         for (int h = 0; h < H && ok; ++h) {
           // P_h written over S buffer h % 2 by all compute warps.
-          if (!(ok = mbar_wait(&c2m_p[h & 1], mph_p[h & 1], p.err, kDevTimeoutOther))) break;
+          if (!(ok = mbar_wait_sleep(&c2m_p[h & 1], mph_p[h & 1], p.err, kDevTimeoutOther))) break;
           mph_p[h & 1] ^= 1;
           tc_fence_after();
           const uint32_t sb = (h & 1) ? kColS1 : kColS0;
@@ -504,7 +508,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (h + 2 < H) {
             // S_{h+2} reuses the columns P_h is read from: wait until P_h.V_h
             // has completed before overwriting them.
-            if (!(ok = mbar_wait(&m2c_o[h & 1], mph_o[h & 1], p.err, kDevTimeoutOther))) break;
+            if (!(ok = mbar_wait_sleep(&m2c_o[h & 1], mph_o[h & 1], p.err, kDevTimeoutOther))) break;
             tc_fence_after();
             issue_s(h + 2);
           }
@@ -534,7 +538,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t ph_g = 0, ph_v = 0, ph_k = 0, ph_s[2] = {0, 0}, ph_o[2] = {0, 0};
     // Warp-uniform outcome: a timeout seen by one lane ends the whole warp.
     auto wait = [&](uint64_t* bar, uint32_t& phase) {
-      const bool ok = __all_sync(0xffffffffu, mbar_wait(bar, phase, p.err, kDevTimeoutAccum));
+      const bool ok = __all_sync(0xffffffffu, mbar_wait_sleep(bar, phase, p.err, kDevTimeoutAccum));
       phase ^= 1;
       tc_fence_after();
       return ok;

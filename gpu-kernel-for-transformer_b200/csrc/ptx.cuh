@@ -101,6 +101,38 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   }
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete
+// sleeps until it completes or kSuspendHintNs pass, instead of returning
+// after the short default limit.
+constexpr uint32_t kSuspendHintNs = 50000;
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
+      : "memory");
+  return ok != 0;
+}
+
+// mbar_wait whose polls sleep (at most kSuspendHintNs each, same overall
+// bound). For kernels whose waiting warps share SM sub-partitions with
+// busy ones: a sleeping poller takes almost no issue slots from them.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, int* err,
+                                                int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (mbar_try_wait_sleep(bar, parity)) return true;
+    if (clock64() - t0 > kWaitLimitCycles) {
+      record_error(err, code);
+      return false;
+    }
+  }
+}
+
 // -------------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
                                             int c0, int c1) {
