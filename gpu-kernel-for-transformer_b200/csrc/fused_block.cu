@@ -191,16 +191,17 @@ __device__ __forceinline__ void tmem_ld_row(uint32_t taddr, float (&v)[32]) {
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
 }
 
-// v += b[0..32) (b in shared memory; every lane reads the same address).
+// v[j] += b[j] for j in [0, 32) (b in shared memory; every lane reads the
+// same address). The elementwise helpers below work on column pairs with
+// f32x2 arithmetic: half the instructions, the same rounding per element.
 __device__ __forceinline__ void add_bias32(float (&v)[32], const float* b) {
   const float4* b4 = reinterpret_cast<const float4*>(b);
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const float4 t = b4[j];
-    v[4 * j] += t.x;
-    v[4 * j + 1] += t.y;
-    v[4 * j + 2] += t.z;
-    v[4 * j + 3] += t.w;
+    f2_unpack(f2_add(f2_pack(v[4 * j], v[4 * j + 1]), f2_pack(t.x, t.y)), v[4 * j], v[4 * j + 1]);
+    f2_unpack(f2_add(f2_pack(v[4 * j + 2], v[4 * j + 3]), f2_pack(t.z, t.w)), v[4 * j + 2],
+              v[4 * j + 3]);
   }
 }
 
@@ -226,20 +227,34 @@ struct Pair {
 // same numbers in the same order.
 __device__ __forceinline__ void row_stats(const float (&x)[2][32], Pair& pr, float eps,
                                           float& mean, float& rstd) {
-  float s4[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums: short dependency chains
+  // Four independent partial sums (columns j mod 4) as two f32x2 pairs:
+  // short dependency chains.
+  uint64_t s01 = f2_pack(0.f, 0.f), s23 = s01;
 #pragma unroll
   for (int c = 0; c < 2; ++c)
 #pragma unroll
-    for (int j = 0; j < 32; ++j) s4[j & 3] += x[c][j];
-  const float m_half = ((s4[0] + s4[1]) + (s4[2] + s4[3])) * (1.0f / 64.0f);
-  float q4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-  for (int c = 0; c < 2; ++c)
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const float t = x[c][j] - m_half;
-      q4[j & 3] = fmaf(t, t, q4[j & 3]);
+    for (int j = 0; j < 32; j += 4) {
+      s01 = f2_add(s01, f2_pack(x[c][j], x[c][j + 1]));
+      s23 = f2_add(s23, f2_pack(x[c][j + 2], x[c][j + 3]));
     }
+  float s4[4];
+  f2_unpack(s01, s4[0], s4[1]);
+  f2_unpack(s23, s4[2], s4[3]);
+  const float m_half = ((s4[0] + s4[1]) + (s4[2] + s4[3])) * (1.0f / 64.0f);
+  const uint64_t mh2 = f2_pack(m_half, m_half);
+  uint64_t q01 = f2_pack(0.f, 0.f), q23 = q01;
+#pragma unroll
+  for (int c = 0; c < 2; ++c)
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      const uint64_t t01 = f2_sub(f2_pack(x[c][j], x[c][j + 1]), mh2);
+      const uint64_t t23 = f2_sub(f2_pack(x[c][j + 2], x[c][j + 3]), mh2);
+      q01 = f2_fma(t01, t01, q01);
+      q23 = f2_fma(t23, t23, q23);
+    }
+  float q4[4];
+  f2_unpack(q01, q4[0], q4[1]);
+  f2_unpack(q23, q4[2], q4[3]);
   const float q = (q4[0] + q4[1]) + (q4[2] + q4[3]);
   const float2 o = pr.swap(make_float2(m_half, q));
   const float m0 = pr.half == 0 ? m_half : o.x, m1 = pr.half == 0 ? o.x : m_half;
@@ -254,6 +269,7 @@ __device__ __forceinline__ void row_stats(const float (&x)[2][32], Pair& pr, flo
 __device__ __forceinline__ void ln_apply(const float (&x)[2][32], float mean, float rstd,
                                          const float* g, const float* b, int half,
                                          float (&v)[2][32]) {
+  const uint64_t mean2 = f2_pack(mean, mean), rstd2 = f2_pack(rstd, rstd);
 #pragma unroll
   for (int c = 0; c < 2; ++c) {
     const int col = 64 * half + 32 * c;
@@ -262,10 +278,15 @@ __device__ __forceinline__ void ln_apply(const float (&x)[2][32], float mean, fl
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const float4 gg = g4[j], bb = b4[j];
-      v[c][4 * j] = (x[c][4 * j] - mean) * rstd * gg.x + bb.x;
-      v[c][4 * j + 1] = (x[c][4 * j + 1] - mean) * rstd * gg.y + bb.y;
-      v[c][4 * j + 2] = (x[c][4 * j + 2] - mean) * rstd * gg.z + bb.z;
-      v[c][4 * j + 3] = (x[c][4 * j + 3] - mean) * rstd * gg.w + bb.w;
+      // ((x - mean) * rstd) * g + b
+      const uint64_t lo = f2_fma(
+          f2_mul(f2_sub(f2_pack(x[c][4 * j], x[c][4 * j + 1]), mean2), rstd2),
+          f2_pack(gg.x, gg.y), f2_pack(bb.x, bb.y));
+      const uint64_t hi = f2_fma(
+          f2_mul(f2_sub(f2_pack(x[c][4 * j + 2], x[c][4 * j + 3]), mean2), rstd2),
+          f2_pack(gg.z, gg.w), f2_pack(bb.z, bb.w));
+      f2_unpack(lo, v[c][4 * j], v[c][4 * j + 1]);
+      f2_unpack(hi, v[c][4 * j + 2], v[c][4 * j + 3]);
     }
   }
 }
@@ -297,10 +318,17 @@ __device__ __forceinline__ void residual_add(uint32_t tl, uint32_t t_acc, int ha
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const float4 bb = b4[j];
-      x[c][4 * j] = __uint_as_float(rx[4 * j]) + (__uint_as_float(ra[4 * j]) + bb.x);
-      x[c][4 * j + 1] = __uint_as_float(rx[4 * j + 1]) + (__uint_as_float(ra[4 * j + 1]) + bb.y);
-      x[c][4 * j + 2] = __uint_as_float(rx[4 * j + 2]) + (__uint_as_float(ra[4 * j + 2]) + bb.z);
-      x[c][4 * j + 3] = __uint_as_float(rx[4 * j + 3]) + (__uint_as_float(ra[4 * j + 3]) + bb.w);
+      // x + (acc + bias)
+      const uint64_t lo = f2_add(
+          f2_pack(__uint_as_float(rx[4 * j]), __uint_as_float(rx[4 * j + 1])),
+          f2_add(f2_pack(__uint_as_float(ra[4 * j]), __uint_as_float(ra[4 * j + 1])),
+                 f2_pack(bb.x, bb.y)));
+      const uint64_t hi = f2_add(
+          f2_pack(__uint_as_float(rx[4 * j + 2]), __uint_as_float(rx[4 * j + 3])),
+          f2_add(f2_pack(__uint_as_float(ra[4 * j + 2]), __uint_as_float(ra[4 * j + 3])),
+                 f2_pack(bb.z, bb.w)));
+      f2_unpack(lo, x[c][4 * j], x[c][4 * j + 1]);
+      f2_unpack(hi, x[c][4 * j + 2], x[c][4 * j + 3]);
     }
 #pragma unroll
     for (int j = 0; j < 32; ++j) rx[j] = __float_as_uint(x[c][j]);
@@ -571,6 +599,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto write_ctx = [&](int h) {
       const float l = psum[((h & 1) * 2 + 0) * kT + r] + psum[((h & 1) * 2 + 1) * kT + r];
       const float inv = l > 0.f ? 1.0f / l : 0.f;
+      const uint64_t inv2 = f2_pack(inv, inv);
       const uint32_t t_o = tl + kColO + (h & 1) * HD + half * HDH;
       float v[HDH];
       if constexpr (HDH == 8) {
@@ -578,7 +607,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld8(t_o, o);
         tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(o[j]) * inv;
+        for (int j = 0; j < 8; j += 2)
+          f2_unpack(f2_mul(f2_pack(__uint_as_float(o[j]), __uint_as_float(o[j + 1])), inv2),
+                    v[j], v[j + 1]);
       } else {
 #pragma unroll
         for (int c = 0; c < HDH / 16; ++c) {
@@ -586,7 +617,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld16(t_o + 16 * c, o);
           tmem_ld_wait();
 #pragma unroll
-          for (int j = 0; j < 16; ++j) v[16 * c + j] = __uint_as_float(o[j]) * inv;
+          for (int j = 0; j < 16; j += 2)
+            f2_unpack(f2_mul(f2_pack(__uint_as_float(o[j]), __uint_as_float(o[j + 1])), inv2),
+                      v[16 * c + j], v[16 * c + j + 1]);
         }
       }
       store_row<HDH / 8>(sA, (h & 1) ? tok1 : tok0, h * HD + half * HDH, v);  // token order
@@ -640,16 +673,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!(ok = wait(m2c_v, ph_v))) break;
         {
           const float bv = lp[kPQkv + 256 + r];  // V bias of feature r
+          const uint64_t bv2 = f2_pack(bv, bv);
           uint32_t ra[32], rb[32];
           tmem_ld32(tl + 256 + 64 * half, ra);
           tmem_ld32(tl + 256 + 64 * half + 32, rb);
           tmem_ld_wait();
           float v[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(ra[j]) + bv;
+          for (int j = 0; j < 32; j += 2)
+            f2_unpack(f2_add(f2_pack(__uint_as_float(ra[j]), __uint_as_float(ra[j + 1])), bv2),
+                      v[j], v[j + 1]);
           store_row<4>(sV, r, 64 * half, v);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(rb[j]) + bv;
+          for (int j = 0; j < 32; j += 2)
+            f2_unpack(f2_add(f2_pack(__uint_as_float(rb[j]), __uint_as_float(rb[j + 1])), bv2),
+                      v[j], v[j + 1]);
           store_row<4>(sV, r, 64 * half + 32, v);
         }
         if (!(ok = wait(m2c_k, ph_k))) break;
