@@ -183,14 +183,6 @@ __device__ __forceinline__ void mma_chain(uint32_t d, uint64_t a_desc, int a_col
                k > 0 ? 1u : 0u);
 }
 
-__device__ __forceinline__ void tmem_ld_row(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  tmem_ld32(taddr, r);
-  tmem_ld_wait();
-#pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-}
-
 // v[j] += b[j] for j in [0, 32) (b in shared memory; every lane reads the
 // same address). The elementwise helpers below work on column pairs with
 // f32x2 arithmetic: half the instructions, the same rounding per element.
@@ -754,19 +746,22 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int i = 0; i < 8; ++i) m8[i] = fmax3(m8[i], sc[i + 24], mx);
               mx = fmaxf(fmax3(m8[0], m8[1], m8[2]), fmax3(fmax3(m8[3], m8[4], m8[5]), m8[6], m8[7]));
             } else {
+              // Masked keys become -inf in the registers pass 2 reads, so
+              // pass 2 needs no mask (exp2(-inf) = 0).
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
                 const int key = k0 + j;
-                if (key >= kl_e && key <= kh_e) mx = fmaxf(mx, sc[j]);
+                const float sv = (key >= kl_e && key <= kh_e) ? sc[j] : -INFINITY;
+                sr[c][j] = __float_as_uint(sv);
+                mx = fmaxf(mx, sv);
               }
             }
           }
           mx = fmaxf(mx, pr.swap(make_float2(mx, 0.f)).x);
           // All keys padding (zero-length sequence): weights exp2(-inf) = 0.
           const float mref = (mx == -INFINITY) ? 0.f : mx * sl2;
-          // Pass 2: exp2, row sum, fp16 packing (f32x2 arithmetic on plain
-          // chunks), from the registers pass 1 loaded.
-          float sum2[2] = {0.f, 0.f};
+          // Pass 2: exp2, row sum, fp16 packing in f32x2 arithmetic, from the
+          // registers pass 1 loaded (and masked).
           uint64_t ls0 = 0, ls1 = 0;
           const uint64_t c2 = f2_pack(sl2, sl2), negm2 = f2_pack(-mref, -mref);
           uint32_t w[32];
@@ -776,33 +771,19 @@ __global__ void __launch_bounds__(kThreads, 1)
               float sc[32];
 #pragma unroll
               for (int j = 0; j < 32; ++j) sc[j] = __uint_as_float(sr[c][j]);
-              const int k0 = 32 * (2 * half + c);
-              if (plain[c]) {
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                  const uint64_t arg = f2_fma(f2_pack(sc[2 * j], sc[2 * j + 1]), c2, negm2);
-                  uint64_t e;
-                  // All on the MUFU unit: at head_dim <= 128 over 128 keys it
-                  // is lightly loaded here (the polynomial offload the
-                  // attention kernel needs would only cost issue slots).
-                  float a0, a1;
-                  f2_unpack(arg, a0, a1);
-                  e = f2_pack(fast_exp2(a0), fast_exp2(a1));
-                  if (j & 1) ls1 = f2_add(ls1, e); else ls0 = f2_add(ls0, e);
-                  float e0, e1;
-                  f2_unpack(e, e0, e1);
-                  w[16 * c + j] = pack_half2(e0, e1);
-                }
-              } else {
-#pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                  float ex = fast_exp2(fmaf(sc[j], sl2, -mref));
-                  if (k0 + j < kl_e || k0 + j > kh_e) ex = 0.f;
-                  sc[j] = ex;
-                  sum2[j & 1] += ex;
-                }
-#pragma unroll
-                for (int j = 0; j < 16; ++j) w[16 * c + j] = pack_half2(sc[2 * j], sc[2 * j + 1]);
+              for (int j = 0; j < 16; ++j) {
+                const uint64_t arg = f2_fma(f2_pack(sc[2 * j], sc[2 * j + 1]), c2, negm2);
+                // All on the MUFU unit: at head_dim <= 128 over 128 keys it is
+                // lightly loaded here (the polynomial offload the attention
+                // kernel needs would only cost issue slots).
+                float a0, a1;
+                f2_unpack(arg, a0, a1);
+                const uint64_t e = f2_pack(fast_exp2(a0), fast_exp2(a1));
+                if (j & 1) ls1 = f2_add(ls1, e); else ls0 = f2_add(ls0, e);
+                float e0, e1;
+                f2_unpack(e, e0, e1);
+                w[16 * c + j] = pack_half2(e0, e1);
               }
             } else {
 #pragma unroll
@@ -812,7 +793,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           float la, lb, lc, ld;
           f2_unpack(ls0, la, lb);
           f2_unpack(ls1, lc, ld);
-          const float sum = (sum2[0] + sum2[1]) + ((la + lb) + (lc + ld));
+          const float sum = (la + lb) + (lc + ld);
           psum[(b * 2 + half) * kT + r] = sum;
           tmem_st32(sb + 64 * half, w);  // P over this warp's own S columns
           tmem_st_wait();
