@@ -20,10 +20,11 @@
 //               variance, softmax max, softmax sums) are merged with the
 //               partner warp through shared memory and a 64-thread barrier.
 //
-// TMEM columns: [0,128) S buffer 0 / Q / out-proj and FFN-out accumulators;
-// [128,256) S buffer 1 / K / FFN-in accumulator; [256,384) V^T accumulator,
-// then the per-head attention outputs O (two buffers), then the fp16 A operand
-// of the FFN GEMMs; [384,512) the fp32 residual stream x of the tile.
+// TMEM columns: [0,128) S buffer 0 / Q; [128,256) S buffer 1 / K / FFN-in
+// accumulator; [256,384) V^T accumulator, then the per-head attention outputs
+// O (two buffers), then the fp16 A operand of the FFN GEMMs; [384,512) the
+// fp32 residual stream x of the tile, onto which the out-proj and FFN-out
+// products accumulate in place (it holds x + that product's bias before).
 //
 // Per layer (c = compute warps, m = MMA thread):
 //   c: LN1(x) -> sA (fp16, K-major, 128B swizzle)
@@ -36,9 +37,9 @@
 //     c: softmax row of S_h -> P_h (fp16, <= 1) written over its own S buffer
 //     m: O_h = P_h . V_h -> O buffer b ; S_{h+2} -> S buffer b
 //     c: (while the MMAs run) ctx_{h-1} = O_{h-1} / rowsum -> sA over Q_{h-1}
-//   m: acc = ctx . Wo^T        c: x += acc + bo; LN2(x) -> TMEM A operand
+//   m: x += ctx . Wo^T         c: LN2(x) -> TMEM A operand; x + b2 -> TMEM x
 //   m: acc = h2 . W1^T         c: g = gelu(acc + b1) -> TMEM A operand
-//   m: acc = g . W2^T          c: x += acc + b2; next LN1 or final LN -> y
+//   m: x += g . W2^T           c: next LN1 (x + next bo -> TMEM x) or final LN -> y
 //
 // Causal balance: TMEM lane quarter q is served by SM sub-partition q, and
 // under a causal mask the last quarter of query rows has four times the work
@@ -173,14 +174,15 @@ __device__ __forceinline__ uint64_t desc_col(uint64_t base_desc, int col) {
 }
 
 // D[128 x N] (+)= A[128 x K] . B[N x K]^T over KSTEPS k-steps of 16 starting
-// at K offsets a_col/b_col (both operands K-major in shared memory).
+// at K offsets a_col/b_col (both operands K-major in shared memory); acc0 = 1
+// adds the first product to what D holds.
 template <int KSTEPS>
 __device__ __forceinline__ void mma_chain(uint32_t d, uint64_t a_desc, int a_col, uint64_t b_desc,
-                                          int b_col, uint32_t idesc) {
+                                          int b_col, uint32_t idesc, uint32_t acc0 = 0u) {
 #pragma unroll
   for (int k = 0; k < KSTEPS; ++k)
     mma_f16_ss(d, desc_col(a_desc, a_col + 16 * k), desc_col(b_desc, b_col + 16 * k), idesc,
-               k > 0 ? 1u : 0u);
+               k > 0 ? 1u : acc0);
 }
 
 // v[j] += b[j] for j in [0, 32) (b in shared memory; every lane reads the
@@ -261,7 +263,8 @@ __device__ __forceinline__ void row_stats(const float (&x)[2][32], Pair& pr, flo
 __device__ __forceinline__ void ln_apply(const float (&x)[2][32], float mean, float rstd,
                                          const float* g, const float* b, int half,
                                          float (&v)[2][32]) {
-  const uint64_t mean2 = f2_pack(mean, mean), rstd2 = f2_pack(rstd, rstd);
+  // (x - mean) * rstd as x * rstd + (-mean * rstd): two FMAs per pair.
+  const uint64_t rstd2 = f2_pack(rstd, rstd), nmr2 = f2_pack(-mean * rstd, -mean * rstd);
 #pragma unroll
   for (int c = 0; c < 2; ++c) {
     const int col = 64 * half + 32 * c;
@@ -270,13 +273,10 @@ __device__ __forceinline__ void ln_apply(const float (&x)[2][32], float mean, fl
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const float4 gg = g4[j], bb = b4[j];
-      // ((x - mean) * rstd) * g + b
-      const uint64_t lo = f2_fma(
-          f2_mul(f2_sub(f2_pack(x[c][4 * j], x[c][4 * j + 1]), mean2), rstd2),
-          f2_pack(gg.x, gg.y), f2_pack(bb.x, bb.y));
-      const uint64_t hi = f2_fma(
-          f2_mul(f2_sub(f2_pack(x[c][4 * j + 2], x[c][4 * j + 3]), mean2), rstd2),
-          f2_pack(gg.z, gg.w), f2_pack(bb.z, bb.w));
+      const uint64_t lo = f2_fma(f2_fma(f2_pack(x[c][4 * j], x[c][4 * j + 1]), rstd2, nmr2),
+                                 f2_pack(gg.x, gg.y), f2_pack(bb.x, bb.y));
+      const uint64_t hi = f2_fma(f2_fma(f2_pack(x[c][4 * j + 2], x[c][4 * j + 3]), rstd2, nmr2),
+                                 f2_pack(gg.z, gg.w), f2_pack(bb.z, bb.w));
       f2_unpack(lo, v[c][4 * j], v[c][4 * j + 1]);
       f2_unpack(hi, v[c][4 * j + 2], v[c][4 * j + 3]);
     }
@@ -295,38 +295,46 @@ __device__ __forceinline__ void store_a_tmem(uint32_t tl, int half, const float 
   tmem_st_wait();
 }
 
-// x[TMEM, this warp's half] += acc + bias; the new values are also returned
-// in registers for the LayerNorm that always follows.
-__device__ __forceinline__ void residual_add(uint32_t tl, uint32_t t_acc, int half,
-                                             const float* bias, float (&x)[2][32]) {
+// TMEM x (this warp's 64 columns) <- x + bias(columns): the starting value
+// of the next in-place product.
+__device__ __forceinline__ void store_x_biased(uint32_t tl, int half, const float* bias,
+                                               const float (&x)[2][32]) {
 #pragma unroll
   for (int c = 0; c < 2; ++c) {
-    const int col = 64 * half + 32 * c;
-    uint32_t ra[32], rx[32];
-    tmem_ld32(t_acc + col, ra);
-    tmem_ld32(tl + kColX + col, rx);
-    tmem_ld_wait();
-    const float4* b4 = reinterpret_cast<const float4*>(bias + col);
+    const float4* b4 = reinterpret_cast<const float4*>(bias + 64 * half + 32 * c);
+    uint32_t o[32];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const float4 bb = b4[j];
-      // x + (acc + bias)
-      const uint64_t lo = f2_add(
-          f2_pack(__uint_as_float(rx[4 * j]), __uint_as_float(rx[4 * j + 1])),
-          f2_add(f2_pack(__uint_as_float(ra[4 * j]), __uint_as_float(ra[4 * j + 1])),
-                 f2_pack(bb.x, bb.y)));
-      const uint64_t hi = f2_add(
-          f2_pack(__uint_as_float(rx[4 * j + 2]), __uint_as_float(rx[4 * j + 3])),
-          f2_add(f2_pack(__uint_as_float(ra[4 * j + 2]), __uint_as_float(ra[4 * j + 3])),
-                 f2_pack(bb.z, bb.w)));
-      f2_unpack(lo, x[c][4 * j], x[c][4 * j + 1]);
-      f2_unpack(hi, x[c][4 * j + 2], x[c][4 * j + 3]);
+      float v0, v1, v2, v3;
+      f2_unpack(f2_add(f2_pack(x[c][4 * j], x[c][4 * j + 1]), f2_pack(bb.x, bb.y)), v0, v1);
+      f2_unpack(f2_add(f2_pack(x[c][4 * j + 2], x[c][4 * j + 3]), f2_pack(bb.z, bb.w)), v2, v3);
+      o[4 * j] = __float_as_uint(v0);
+      o[4 * j + 1] = __float_as_uint(v1);
+      o[4 * j + 2] = __float_as_uint(v2);
+      o[4 * j + 3] = __float_as_uint(v3);
     }
-#pragma unroll
-    for (int j = 0; j < 32; ++j) rx[j] = __float_as_uint(x[c][j]);
-    tmem_st32(tl + kColX + col, rx);
+    tmem_st32(tl + kColX + 64 * half + 32 * c, o);
   }
   tmem_st_wait();
+}
+
+// The out-proj and FFN-out products accumulate in place onto the residual
+// stream x in TMEM, which holds x + bias of that product beforehand. This
+// reads this warp's half of the updated x into registers (for the LayerNorm
+// that always follows) and, when next_bias is given, stores x + next_bias back
+// for the next in-place product.
+__device__ __forceinline__ void residual_read(uint32_t tl, int half, const float* next_bias,
+                                              float (&x)[2][32]) {
+  uint32_t rx[2][32];
+#pragma unroll
+  for (int c = 0; c < 2; ++c) tmem_ld32(tl + kColX + 64 * half + 32 * c, rx[c]);
+  tmem_ld_wait();
+#pragma unroll
+  for (int c = 0; c < 2; ++c)
+#pragma unroll
+    for (int j = 0; j < 32; ++j) x[c][j] = __uint_as_float(rx[c][j]);
+  if (next_bias != nullptr) store_x_biased(tl, half, next_bias, x);
 }
 
 template <int HD>
@@ -474,13 +482,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     };
     // D = A . W^T, A the fp16 operand in TMEM A columns.
-    auto gemm_tmem_a = [&](uint32_t dcol) {
+    auto gemm_tmem_a = [&](uint32_t dcol, uint32_t acc0) {
       uint64_t w;
       if (!take_w(w)) return false;
 #pragma unroll
       for (int k = 0; k < kT / 16; ++k)
         mma_f16_ts(tmem + dcol, tmem + kColA + 8 * k, desc_col(w, 16 * k), id128,
-                   k > 0 ? 1u : 0u);
+                   k > 0 ? 1u : acc0);
       release_w();
       return true;
     };
@@ -536,14 +544,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!ok || !(ok = wait_c2m())) break;  // ctx complete in sA
         if (!(ok = take_w(w))) break;
-        mma_chain<kT / 16>(tmem + 0, dA, 0, w, 0, id128);  // out-proj
+        mma_chain<kT / 16>(tmem + kColX, dA, 0, w, 0, id128, 1u);  // x += out-proj
         release_w();
         mma_commit(m2c_g);
         if (!(ok = wait_c2m())) break;  // LN2 output in TMEM A
-        if (!(ok = gemm_tmem_a(kColF))) break;
+        if (!(ok = gemm_tmem_a(kColF, 0u))) break;
         mma_commit(m2c_g);
         if (!(ok = wait_c2m())) break;  // GELU output in TMEM A
-        if (!(ok = gemm_tmem_a(0))) break;
+        if (!(ok = gemm_tmem_a(kColX, 1u))) break;  // x += FFN-out
         mma_commit(m2c_g);
       }
     }
@@ -634,7 +642,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float4* x4 = reinterpret_cast<const float4*>(p.x + grow * kT + 64 * half);
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
-          uint32_t o[32];
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             const float4 t = row_ok ? __ldcs(x4 + 8 * c + j) : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -643,11 +650,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             xv[c][4 * j + 2] = t.z;
             xv[c][4 * j + 3] = t.w;
           }
-#pragma unroll
-          for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(xv[c][j]);
-          tmem_st32(tl + kColX + 64 * half + 32 * c, o);
         }
-        tmem_st_wait();
+        store_x_biased(tl, half, par + kPOut, xv);  // layer 0's out-proj adds onto x + bo
       }
       {
         float mean, rstd, v[2][32];
@@ -747,14 +751,24 @@ __global__ void __launch_bounds__(kThreads, 1)
               mx = fmaxf(fmax3(m8[0], m8[1], m8[2]), fmax3(fmax3(m8[3], m8[4], m8[5]), m8[6], m8[7]));
             } else {
               // Masked keys become -inf in the registers pass 2 reads, so
-              // pass 2 needs no mask (exp2(-inf) = 0).
+              // pass 2 needs no mask (exp2(-inf) = 0). In a tile of one
+              // unpadded sequence only the causal bound can cut a chunk.
+              const int jlo = kl_e - k0, jhi = kh_e - k0;
+              if (plain_tile) {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const int key = k0 + j;
-                const float sv = (key >= kl_e && key <= kh_e) ? sc[j] : -INFINITY;
-                sr[c][j] = __float_as_uint(sv);
-                mx = fmaxf(mx, sv);
+                for (int j = 0; j < 32; ++j) sc[j] = j <= jhi ? sc[j] : -INFINITY;
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) sc[j] = (j >= jlo && j <= jhi) ? sc[j] : -INFINITY;
               }
+#pragma unroll
+              for (int j = 0; j < 32; ++j) sr[c][j] = __float_as_uint(sc[j]);
+              float m8[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) m8[i] = fmax3(sc[i], sc[i + 8], sc[i + 16]);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) m8[i] = fmax3(m8[i], sc[i + 24], mx);
+              mx = fmaxf(fmax3(m8[0], m8[1], m8[2]), fmax3(fmax3(m8[3], m8[4], m8[5]), m8[6], m8[7]));
             }
           }
           mx = fmaxf(mx, pr.swap(make_float2(mx, 0.f)).x);
@@ -812,7 +826,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!(ok = wait(m2c_g, ph_g))) break;  // out-proj accumulator
         {
           float mean, rstd, v[2][32];
-          residual_add(tl, tl, half, lp + kPOut, xv);
+          residual_read(tl, half, lp + kPFo, xv);  // x + out-proj; store x + b2
           row_stats(xv, pr, p.eps, mean, rstd);
           ln_apply(xv, mean, rstd, lp + kPLn2g, lp + kPLn2b, half, v);
           store_a_tmem(tl, half, v);
@@ -846,7 +860,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!(ok = wait(m2c_g, ph_g))) break;  // FFN-out accumulator
         {
           float mean, rstd, v[2][32];
-          residual_add(tl, tl, half, lp + kPFo, xv);
+          residual_read(tl, half, l + 1 < L ? lp + kParFloats + kPOut : nullptr, xv);
           row_stats(xv, pr, p.eps, mean, rstd);
           if (l + 1 < L) {
             ln_apply(xv, mean, rstd, lp + kParFloats + kPLn1g, lp + kParFloats + kPLn1b, half,
