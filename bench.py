@@ -493,8 +493,6 @@ def main():
                                 device_id=dev)
     pkg = importlib.import_module("gpu-kernel-for-transformer_b200")
     lib = pkg._lib.load()
-    if args.chain:
-        lib.tfx_set_fused_policy(0)
 
     B, S, D, H, F, L = CONFIGS[args.config]
     if args.batch:
@@ -504,6 +502,7 @@ def main():
     cfg = pkg.TransformerConfig(B, S, D, H, F, L, True)
     torch.manual_seed(SEED)
     model = pkg.UserOptimizedTransformer(cfg).to(dev).eval()
+    model.enable_fused_forward(not args.chain)
     x_host = make_input(B, S, D, SEED + 100000 + rank)
     x = x_host.to(dev)
     y = torch.empty_like(x)

@@ -29,6 +29,9 @@ TFX_ERR_DEVICE = -6
 TFX_DTYPE_F16 = 0
 TFX_DTYPE_F32 = 1
 
+TFX_PATH_AUTO = 0
+TFX_PATH_CHAIN = 1
+
 TFX_EPI_BIAS = 0
 TFX_EPI_BIAS_GELU = 1
 TFX_EPI_BIAS_RESIDUAL = 2
@@ -49,7 +52,6 @@ SIGNATURES = {
     "tfx_attention_vt_ld": (_I64, [_I]),
     "tfx_transpose_v": (_I, [_P, _I64, _P, _I, _I, _I, _P]),
     "tfx_attention_vt": (_I, [_P, _P, _P, _I64, _P, _I64, _I, _I, _I, _I, _F, _I, _P, _P]),
-    "tfx_set_fused_policy": (_I, [_I]),
     "tfx_forward_workspace_bytes": (_I64, [_P, _I, _I]),
     "tfx_forward": (_I, [_P, _P, _P, _I, _I, _P, _P, ctypes.c_size_t, _P]),
     "tfx_forward_static": (_I, [_P, _P, _P, _I, _I, _P, _P]),
@@ -85,6 +87,7 @@ class TfxModel(ctypes.Structure):
         ("layers", ctypes.POINTER(TfxLayer)),
         ("final_norm_weight", ctypes.c_void_p),
         ("final_norm_bias", ctypes.c_void_p),
+        ("path", ctypes.c_int),
     ]
 
 

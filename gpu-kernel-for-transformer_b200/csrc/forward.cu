@@ -60,10 +60,17 @@ __global__ void kv_append_kernel(const __half* __restrict__ qkv, int64_t ld_qkv,
 }
 
 constexpr size_t kAlign = 256;
-int g_fused_policy = 1;  // 1: fused whole-forward kernel where it applies; 0: per-op chain
 
+// The model's own path setting decides (tfx_model.path); nothing here is
+// process-wide.
 bool use_fused(const tfx_model* m, int seq, const int32_t* valid_len) {
-  return g_fused_policy != 0 && fused_forward_supported(m, seq, valid_len);
+  return m->path == TFX_PATH_AUTO && fused_forward_supported(m, seq, valid_len);
+}
+
+// [a, a + a_bytes) and [b, b + b_bytes) share at least one byte.
+bool ranges_overlap(const void* a, size_t a_bytes, const void* b, size_t b_bytes) {
+  const uintptr_t a0 = reinterpret_cast<uintptr_t>(a), b0 = reinterpret_cast<uintptr_t>(b);
+  return a0 < b0 + b_bytes && b0 < a0 + a_bytes;
 }
 
 size_t round_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
@@ -113,6 +120,9 @@ Workspace plan_workspace(char* base, int batch, int seq, int d, int f, int hd,
 int check_model(const tfx_model* mdl) {
   if (mdl == nullptr || mdl->layers == nullptr)
     return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward: null model");
+  if (mdl->path != TFX_PATH_AUTO && mdl->path != TFX_PATH_CHAIN)
+    return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward: model path %d is not a tfx_path",
+                mdl->path);
   const int d = mdl->d_model, h = mdl->num_heads, f = mdl->ffn_dim;
   if (d <= 0 || h <= 0 || f <= 0 || mdl->num_layers <= 0)
     return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward: model sizes must be positive");
@@ -234,12 +244,6 @@ using namespace tfx;
 
 extern "C" {
 
-int tfx_set_fused_policy(int enable) {
-  const int prev = g_fused_policy;
-  g_fused_policy = enable ? 1 : 0;
-  return prev;
-}
-
 int64_t tfx_forward_workspace_bytes(const tfx_model* model, int batch, int seq) {
   if (check_model(model) != TFX_OK || batch <= 0 || seq <= 0) return -1;
   if (use_fused(model, seq, nullptr)) return 0;
@@ -257,7 +261,9 @@ int tfx_forward(const tfx_model* model, const float* x, float* y, int batch, int
     return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward: null x or y");
   if (batch <= 0 || seq <= 0)
     return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward: batch and seq must be positive");
-  if (x == y) return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward: y must not alias x");
+  const size_t act_bytes = sizeof(float) * static_cast<size_t>(batch) * seq * model->d_model;
+  if (ranges_overlap(x, act_bytes, y, act_bytes))
+    return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward: y must not overlap x");
   if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(y) % 16 ||
       reinterpret_cast<uintptr_t>(workspace) % kAlign)
     return fail(TFX_ERR_MISALIGNED, "tfx_forward: x/y 16-byte and workspace 256-byte alignment");
@@ -299,7 +305,10 @@ int tfx_forward_kv(const tfx_model* model, const float* x, float* y, int batch, 
   if (static_cast<int64_t>(cache_len) + new_tokens > capacity)
     return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward_kv: KV cache capacity exceeded (%lld > %d)",
                 static_cast<long long>(cache_len) + new_tokens, capacity);
-  if (x == y) return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward_kv: y must not alias x");
+  const size_t act_bytes = sizeof(float) * static_cast<size_t>(batch) * new_tokens *
+                           model->d_model;
+  if (ranges_overlap(x, act_bytes, y, act_bytes))
+    return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward_kv: y must not overlap x");
   if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(y) % 16 ||
       reinterpret_cast<uintptr_t>(k_cache) % 16 || reinterpret_cast<uintptr_t>(v_cache) % 16 ||
       reinterpret_cast<uintptr_t>(workspace) % kAlign)

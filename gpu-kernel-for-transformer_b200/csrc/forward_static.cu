@@ -22,9 +22,10 @@
 // * Nothing in the array has to start at zero: every byte the kernels read
 //   was written earlier in the same forward, so the previous call's leftover
 //   contents are harmless.
-// * The first call on each device resolves the array's device address
-//   (cudaGetSymbolAddress) with that device current; make that first call
-//   before any stream capture begins.
+// * The first call on each device that runs the per-op chain resolves the
+//   array's device address (cudaGetSymbolAddress) with that device current;
+//   make that first call before any stream capture begins. Calls the fused
+//   whole-forward kernel serves need no scratch and skip the lookup.
 #include <mutex>
 
 #include "internal.h"
@@ -75,6 +76,10 @@ int tfx_forward_static(const tfx_model* model, const float* x, float* y, int bat
                 "tfx_forward_static: batch=%d seq=%d needs %lld bytes of scratch, more than the "
                 "library's fixed %zu-byte array; use tfx_forward with a caller workspace",
                 batch, seq, static_cast<long long>(need), kStaticScratchBytes);
+  // The fused whole-forward kernel keeps every intermediate on chip: no
+  // scratch, so no symbol lookup either.
+  if (need == 0)
+    return tfx_forward(model, x, y, batch, seq, valid_len, nullptr, 0, stream);
   void* scratch = nullptr;
   const int st = scratch_for_current_device(&scratch);
   if (st != TFX_OK) return st;

@@ -5,9 +5,11 @@ names/layout, toggles and ``forward(x, valid_token_mask)`` contract
 
 ``UserOptimizedTransformer.forward`` makes ONE call into the native runtime
 (``tfx_forward`` in lib/libtfx_b200.so), which enqueues every kernel of the
-forward on the current stream. Nothing here computes on the CPU: a CPU input
-raises (the reference's CPU fallback, torch_transformer_benchmark.py:1003-1006,
-is deliberately not reproduced), as does a missing library.
+forward on the current stream. UserOptimizedTransformer never computes on the
+CPU: a CPU input raises (the reference's CPU fallback,
+torch_transformer_benchmark.py:1003-1006, is deliberately not reproduced), as
+does a missing library. BaselineTransformer is the explicit eager model, for
+any device.
 """
 
 from __future__ import annotations
@@ -19,6 +21,7 @@ from typing import Dict, Optional, Tuple
 
 import torch
 import torch.nn as nn
+import torch.nn.functional as F
 
 from . import _lib
 
@@ -75,9 +78,10 @@ OFFICIAL_BENCHMARK_SHAPES: Dict[int, TransformerConfig] = {
 }
 
 
-class _SelfAttentionParams(nn.Module):
-    """Parameter container with BaselineSelfAttention's names and creation
-    order (torch_transformer_benchmark.py:207-220)."""
+class _SelfAttention(nn.Module):
+    """Multi-head self-attention with BaselineSelfAttention's parameter names
+    and creation order (torch_transformer_benchmark.py:204-220), and its
+    explicit FP32 eager forward (:222-267)."""
 
     def __init__(self, d_model: int, num_heads: int) -> None:
         super().__init__()
@@ -92,27 +96,59 @@ class _SelfAttentionParams(nn.Module):
         self.v_proj = nn.Linear(d_model, d_model, bias=True)
         self.out_proj = nn.Linear(d_model, d_model, bias=True)
 
+    def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None,
+                causal: bool = False) -> torch.Tensor:
+        b, s, _ = x.shape
 
-class _BlockParams(nn.Module):
-    """BaselineTransformerBlock's parameters (torch_transformer_benchmark.py:270-277)."""
+        def by_head(t: torch.Tensor) -> torch.Tensor:  # [B, S, D] -> [B, H, S, hd]
+            return t.view(b, s, self.num_heads, self.head_dim).transpose(1, 2)
+
+        q, k, v = by_head(self.q_proj(x)), by_head(self.k_proj(x)), by_head(self.v_proj(x))
+        scores = torch.matmul(q, k.transpose(-2, -1)) * self.scale
+        if causal:
+            later = torch.ones(s, s, dtype=torch.bool, device=x.device).triu(1)
+            scores = scores.masked_fill(later, float("-inf"))
+        if valid_token_mask is not None:  # padded keys, per sequence
+            scores = scores.masked_fill(~valid_token_mask[:, None, None, :], float("-inf"))
+        weights = torch.softmax(scores.float(), dim=-1).to(x.dtype)
+        ctx = torch.matmul(weights, v).transpose(1, 2).reshape(b, s, self.d_model)
+        out = self.out_proj(ctx)
+        if valid_token_mask is not None:
+            out = out.masked_fill(~valid_token_mask[..., None], 0)
+        return out
+
+
+class _Block(nn.Module):
+    """Pre-norm block with BaselineTransformerBlock's parameters
+    (torch_transformer_benchmark.py:270-277) and forward (:279-290): exact
+    (erf) GELU, padded rows zeroed after the block."""
 
     def __init__(self, d_model: int, num_heads: int, ffn_dim: int) -> None:
         super().__init__()
         self.norm1 = nn.LayerNorm(d_model)
-        self.attention = _SelfAttentionParams(d_model, num_heads)
+        self.attention = _SelfAttention(d_model, num_heads)
         self.norm2 = nn.LayerNorm(d_model)
         self.ffn_in = nn.Linear(d_model, ffn_dim)
         self.ffn_out = nn.Linear(ffn_dim, d_model)
 
+    def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor],
+                causal: bool) -> torch.Tensor:
+        x = x + self.attention(self.norm1(x), valid_token_mask, causal)
+        x = x + self.ffn_out(F.gelu(self.ffn_in(self.norm2(x)), approximate="none"))
+        if valid_token_mask is not None:
+            x = x.masked_fill(~valid_token_mask[..., None], 0)
+        return x
+
 
 class BaselineTransformer(nn.Module):
-    """The reference model's module tree (torch_transformer_benchmark.py:293-305).
+    """The reference's explicit model (torch_transformer_benchmark.py:293-317).
 
     Constructing it under ``torch.manual_seed(s)`` draws exactly the weights
     the reference draws, and its state_dict keys are the reference's, so
-    ``load_state_dict`` of a reference checkpoint works unchanged. This
-    package ships only the B200 path: the explicit FP32 eager forward is the
-    reference's own code and is not duplicated here.
+    ``load_state_dict`` of a reference checkpoint works unchanged. Its forward
+    is the plain eager PyTorch computation in the parameters' dtype (FP32 by
+    default) on any device: the accuracy baseline the reference's harness
+    compares the optimized module against, and the CPU path.
     """
 
     def __init__(self, config: TransformerConfig) -> None:
@@ -120,17 +156,20 @@ class BaselineTransformer(nn.Module):
         self.config = config
         self.layers = nn.ModuleList(
             [
-                _BlockParams(config.d_model, config.num_heads, config.ffn_dim)
+                _Block(config.d_model, config.num_heads, config.ffn_dim)
                 for _ in range(config.num_layers)
             ]
         )
         self.final_norm = nn.LayerNorm(config.d_model)
 
-    def forward(self, x, valid_token_mask=None):  # pragma: no cover - documented stub
-        raise NotImplementedError(
-            "this package provides only the CUDA path (UserOptimizedTransformer); the "
-            "explicit FP32 baseline forward is the reference implementation's"
-        )
+    def forward(self, x: torch.Tensor,
+                valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+        for layer in self.layers:
+            x = layer(x, valid_token_mask, self.config.causal)
+        x = self.final_norm(x)
+        if valid_token_mask is not None:
+            x = x.masked_fill(~valid_token_mask[..., None], 0)
+        return x
 
 
 @dataclass(frozen=True)
@@ -189,6 +228,7 @@ class UserOptimizedTransformer(BaselineTransformer):
         self._packed = None  # (key, tensors, ctypes structs)
         self._workspace: Dict[torch.device, torch.Tensor] = {}
         self._mask_cache = None
+        self._path = _lib.TFX_PATH_AUTO
 
     # ------------------------------------------------------------ toggles
     @property
@@ -223,6 +263,16 @@ class UserOptimizedTransformer(BaselineTransformer):
         tcgen05 GEMM with the fused GELU epilogue."""
         if not enabled:
             raise NotImplementedError("the native path has no unfused FFN fallback")
+
+    def enable_fused_forward(self, enabled: bool = True) -> None:
+        """Per-module choice of kernels, like the reference's per-module
+        ``enable_triton_fused_*`` toggles (torch_transformer_benchmark.py
+        :379-393): True (default) runs the whole forward as one fused kernel
+        where it applies (d_model = ffn_dim = 128, seq_len dividing 128),
+        False always runs the per-op kernel chain. Only this module changes."""
+        self._path = _lib.TFX_PATH_AUTO if enabled else _lib.TFX_PATH_CHAIN
+        if self._packed is not None:
+            self._packed[3].path = self._path
 
     def enable_attention_fp16_accumulation(self, enabled: bool = True) -> None:
         """torch_transformer_benchmark.py:395-407: fp16 accumulation is never
@@ -306,9 +356,28 @@ class UserOptimizedTransformer(BaselineTransformer):
 
     # ---------------------------------------------------------- packing
     def _param_key(self, device: torch.device) -> Tuple:
+        """Identity of the parameters as packed: storage address, version
+        counter and dtype of each. Inference tensors expose no version
+        counter; for them a content fingerprint (sum and sum of squares of
+        all parameters, read back once per forward) stands in, so an
+        in-place update inside ``torch.inference_mode()`` still repacks and an
+        unchanged model is not re-uploaded on every call. During CUDA graph
+        capture (no host reads allowed) the addresses alone decide."""
         key = [device]
+        versionless = []
         for p in self.parameters():
-            key.append((p.data_ptr(), _version(p), p.dtype))
+            ver = _version(p)
+            key.append((p.data_ptr(), ver, p.dtype))
+            if ver is None:
+                versionless.append(p)
+        if versionless:
+            if torch.cuda.is_available() and torch.cuda.is_current_stream_capturing():
+                key.append("capturing")
+            else:
+                with torch.no_grad():
+                    flat = torch.cat([p.detach().reshape(-1).double() for p in versionless])
+                    fp = torch.stack((flat.sum(), flat.square().sum())).tolist()
+                key.append(tuple(fp))
         return tuple(key)
 
     def _prepare(self, device: torch.device):
@@ -316,8 +385,9 @@ class UserOptimizedTransformer(BaselineTransformer):
         version-checked caches, torch_transformer_benchmark.py:524-655):
         fp16 [out, in] GEMM weights (q|k|v stacked), fp32 biases and norms."""
         key = self._param_key(device)
-        if self._packed is not None and self._packed[0] == key and \
-                all(k[1] is not None for k in key[1:]):
+        if self._packed is not None and (
+                self._packed[0] == key
+                or (key[-1] == "capturing" and self._packed[0][:-1] == key[:-1])):
             return self._packed
         keep = []
 
@@ -358,6 +428,7 @@ class UserOptimizedTransformer(BaselineTransformer):
         model.layers = ctypes.cast(layers, ctypes.POINTER(_lib.TfxLayer))
         model.final_norm_weight = f32(self.final_norm.weight)
         model.final_norm_bias = f32(self.final_norm.bias)
+        model.path = self._path
         self._packed = (key, keep, layers, model)
         return self._packed
 

@@ -154,6 +154,14 @@ typedef struct tfx_layer {
   const float* ffn_out_bias;      /* [D] */
 } tfx_layer;
 
+/* Which kernels tfx_forward runs for a model (tfx_model.path). */
+typedef enum tfx_path {
+  TFX_PATH_AUTO = 0,  /* fused whole-forward kernel wherever it applies (d_model =
+                         ffn_dim = 128, seq_len dividing 128, head_dim in
+                         {16, 32, 64, 128}, <= 5 layers), else the per-op chain */
+  TFX_PATH_CHAIN = 1  /* always the per-op kernel chain */
+} tfx_path;
+
 typedef struct tfx_model {
   int d_model;
   int num_heads;
@@ -164,26 +172,21 @@ typedef struct tfx_model {
   const tfx_layer* layers;     /* HOST array of num_layers entries         */
   const float* final_norm_weight;
   const float* final_norm_bias;
+  /* tfx_path of this model (zero-initialised structs get TFX_PATH_AUTO).
+   * A per-model setting, like the reference's per-module toggles
+   * enable_triton_fused_norm / _ffn (torch_transformer_benchmark.py:379-393):
+   * two models in one process never change each other's kernels. Query
+   * tfx_forward_workspace_bytes again after changing it. */
+  int path;
 } tfx_model;
 
-/*
- * Path policy of tfx_forward for this process: 1 (default) runs the fused
- * whole-forward kernel wherever it applies (d_model = ffn_dim = 128, seq_len
- * dividing 128, head_dim in {16, 32, 64, 128}, <= 5 layers; with or without
- * valid_len); 0 always runs the per-op kernel chain. Returns the previous
- * policy. Query tfx_forward_workspace_bytes again after changing it.
- * No reference counterpart (the reference's toggles are per-module:
- * enable_triton_fused_norm / _ffn, torch_transformer_benchmark.py:379-393).
- */
-TFX_API int tfx_set_fused_policy(int enable);
-
 /* Bytes of device workspace tfx_forward needs for a [batch, seq] input
- * (0 when the fused whole-forward kernel applies). */
+ * (0 when the fused whole-forward kernel applies to this model and path). */
 TFX_API int64_t tfx_forward_workspace_bytes(const tfx_model* model, int batch, int seq);
 
 /*
  * Whole forward: y = final_norm(blocks(x)), x and y [batch, seq, D] fp32
- * (y must not alias x). valid_len: NULL or [batch] int32 prefix lengths
+ * (the two ranges must not overlap: TFX_ERR_INVALID_ARGUMENT). valid_len: NULL or [batch] int32 prefix lengths
  * (padded rows of y are zeroed, padded keys masked). workspace: device
  * buffer of at least tfx_forward_workspace_bytes() (may be NULL when that
  * is 0).

@@ -89,6 +89,32 @@ def test_forward_rejects_bad_models(lib):
     assert lib.tfx_forward_workspace_bytes(ctypes.byref(m), 1, 1) == -1
 
 
+def test_forward_rejects_overlap_and_bad_path(lib):
+    """x and y ranges must be disjoint (not only different pointers), and the
+    model's path must be a tfx_path; both checked on the host."""
+    pkg = load_package()
+    L = pkg._lib
+    m = L.TfxModel()
+    m.d_model, m.num_heads, m.ffn_dim, m.num_layers, m.causal, m.eps = 128, 4, 128, 1, 1, 1e-5
+    layers = (L.TfxLayer * 1)()
+    for f, _ in L.TfxLayer._fields_:
+        setattr(layers[0], f, 256)
+    m.layers = ctypes.cast(layers, ctypes.POINTER(L.TfxLayer))
+    m.final_norm_weight = m.final_norm_bias = 256
+    x = 1 << 20
+    # y starts half-way into x's 2 x 8 x 128 floats
+    st = lib.tfx_forward(ctypes.byref(m), ctypes.c_void_p(x), ctypes.c_void_p(x + 4096), 2, 8,
+                         None, None, 0, None)
+    assert st == L.TFX_ERR_INVALID_ARGUMENT
+    assert b"overlap" in lib.tfx_last_error_message()
+    m.path = 7
+    assert lib.tfx_forward_workspace_bytes(ctypes.byref(m), 2, 8) == -1
+    st = lib.tfx_forward(ctypes.byref(m), ctypes.c_void_p(x), ctypes.c_void_p(x + 8192), 2, 8,
+                         None, None, 0, None)
+    assert st == L.TFX_ERR_INVALID_ARGUMENT
+    assert b"path" in lib.tfx_last_error_message()
+
+
 def test_workspace_size_formula(lib):
     pkg = load_package()
     L = pkg._lib
@@ -103,11 +129,9 @@ def test_workspace_size_formula(lib):
     per_row = 2 * 128 + 2 * 384 + 2 * 128 + 4 * 128 + 2 * 128
     # D = F = 128, seq | 128: the fused whole-forward kernel needs no workspace
     assert lib.tfx_forward_workspace_bytes(ctypes.byref(m), 10, 128) == 0
-    prev = lib.tfx_set_fused_policy(0)
-    try:
-        need = lib.tfx_forward_workspace_bytes(ctypes.byref(m), 10, 128)
-    finally:
-        lib.tfx_set_fused_policy(prev)
+    m.path = L.TFX_PATH_CHAIN
+    need = lib.tfx_forward_workspace_bytes(ctypes.byref(m), 10, 128)
+    m.path = L.TFX_PATH_AUTO
     # h, qkv, ctx (fp16, D, 3D, D) + residual (fp32, D) + ffn hidden (fp16, F)
     assert need == rows * per_row
     # seq not dividing 128: the per-op chain and its workspace

@@ -167,15 +167,12 @@ def test_fused_forward_and_op_chain_match_oracle(pkg, dev, case):
     lib = pkg._lib.load()
     _, _, _, mdl = cand._prepare(dev)
     outs = {}
-    try:
-        for policy in (1, 0):
-            lib.tfx_set_fused_policy(policy)
-            need = lib.tfx_forward_workspace_bytes(ctypes.byref(mdl), b, s)
-            assert (need == 0) == (policy == 1), need
-            with torch.inference_mode():
-                outs[policy] = cand(x.to(dev), mask.to(dev)).cpu()
-    finally:
-        lib.tfx_set_fused_policy(1)
+    for policy in (1, 0):
+        cand.enable_fused_forward(bool(policy))
+        need = lib.tfx_forward_workspace_bytes(ctypes.byref(mdl), b, s)
+        assert (need == 0) == (policy == 1), need
+        with torch.inference_mode():
+            outs[policy] = cand(x.to(dev), mask.to(dev)).cpu()
     with torch.inference_mode():
         ref = oracle_model(x, mask)
     for policy, y in outs.items():

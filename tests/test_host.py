@@ -97,9 +97,60 @@ def test_no_cpu_fallback(pkg):
     m = pkg.UserOptimizedTransformer(pkg.TransformerConfig(1, 8, 128, 4, 128, 1, True))
     with pytest.raises(RuntimeError):
         m(torch.zeros(1, 8, 128))
-    with pytest.raises(NotImplementedError):
-        pkg.BaselineTransformer(pkg.TransformerConfig(1, 8, 128, 4, 128, 1, True))(
-            torch.zeros(1, 8, 128))
+
+
+@pytest.mark.parametrize("name", ["c1", "padded_c1", "ragged_s37", "noncausal_small", "c4_b2"])
+def test_package_baseline_forward_matches_golden(pkg, name):
+    """The package's own BaselineTransformer (eager FP32, no oracle import)
+    reproduces the reference's recorded outputs, masks included."""
+    rec = load_golden(name)
+    cfg = pkg.TransformerConfig(**rec["config"])
+    torch.manual_seed(rec["model_seed"])
+    model = pkg.BaselineTransformer(cfg).eval()
+    assert ob.state_dict_checksum(model) == rec["state_sha256"]
+    x, mask = ob.generate_random_case(ob.TransformerConfig(**rec["config"]), rec["input_seed"],
+                                      rec["padding_ratio"])
+    with torch.inference_mode():
+        y = model(x, mask)
+    assert torch.allclose(y, rec["output"], atol=2e-5, rtol=0), (y - rec["output"]).abs().max()
+
+
+def test_package_baseline_forward_equals_oracle_on_holes(pkg):
+    """Arbitrary (non-prefix) masks: the package baseline and the oracle agree."""
+    cfg = dict(batch_size=3, seq_len=20, d_model=64, num_heads=4, ffn_dim=96, num_layers=2,
+               causal=True)
+    oracle_model = ob.make_baseline(ob.TransformerConfig(**cfg), 3)
+    torch.manual_seed(3)
+    model = pkg.BaselineTransformer(pkg.TransformerConfig(**cfg)).eval()
+    x = torch.randn(3, 20, 64, generator=torch.Generator().manual_seed(4))
+    mask = torch.rand(3, 20, generator=torch.Generator().manual_seed(5)) > 0.3
+    mask[:, 0] = True
+    with torch.inference_mode():
+        assert torch.allclose(model(x, mask), oracle_model(x, mask), atol=1e-6, rtol=0)
+
+
+def test_fused_toggle_is_per_module(pkg):
+    cfg = pkg.TransformerConfig(2, 16, 64, 4, 96, 1, True)
+    a = pkg.UserOptimizedTransformer(cfg)
+    b = pkg.UserOptimizedTransformer(cfg)
+    a.enable_fused_forward(False)
+    assert a._prepare(torch.device("cpu"))[3].path == pkg._lib.TFX_PATH_CHAIN
+    assert b._prepare(torch.device("cpu"))[3].path == pkg._lib.TFX_PATH_AUTO
+    a.enable_fused_forward(True)
+    assert a._prepare(torch.device("cpu"))[3].path == pkg._lib.TFX_PATH_AUTO
+
+
+def test_inference_tensor_parameters_pack_once_and_repack_on_change(pkg):
+    """Parameters created under inference_mode have no version counter: the
+    packed weights are reused while their contents are unchanged and rebuilt
+    after an in-place update."""
+    cfg = pkg.TransformerConfig(2, 16, 64, 4, 96, 1, True)
+    with torch.inference_mode():
+        m = pkg.UserOptimizedTransformer(cfg)
+        first = m._prepare(torch.device("cpu"))
+        assert m._prepare(torch.device("cpu")) is first
+        m.layers[0].ffn_out.weight.mul_(2.0)
+        assert m._prepare(torch.device("cpu")) is not first
 
 
 def test_toggles_keep_reference_contract(pkg):
