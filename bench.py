@@ -23,9 +23,18 @@ reference's own distribution). One step = one full forward of that batch.
 * cpu_baseline: the FP32 oracle (restatement of the reference's
   BaselineTransformer) on the host cores, rank 0 at N=1, bounded sample.
 
-Multi-GPU: one process per GPU (torchrun); every rank runs its own
-B-sequence shard (weak scaling) with no collective in the timed region; the
-outputs are gathered to rank 0 once afterwards (timed separately).
+Multi-GPU: one process per GPU (torchrun); the config's global batch is
+split into contiguous per-rank shards (strong scaling: c2 at 8 GPUs is 1250
+sequences per rank) with no collective in the timed region; the outputs are
+gathered to rank 0 once afterwards (timed separately). Sequence b of every
+config's input is drawn from its own seed, so the global input is the same at
+every GPU count.
+
+per_config: the same measurement (value, roofline, e2e, accuracy) for the
+other BASELINE configs c1, c3, c4 and c5 (c5: the full B=32, S=100000 batch,
+sharded like the headline; no e2e, whose pinned buffers would be 26 GB).
+accuracy: a seeded sample of the output compared off the clock with the FP32
+oracle under the reference's elementwise rule (failed-element count).
 
 `--impl reference` times the reference's CPU implementation of the path (the
 oracle port: the reference is pure PyTorch and its CPU path is
@@ -76,6 +85,7 @@ def parse_args():
                     help="wall-clock budget of the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-accuracy", action="store_true")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the per-GPU batch (small cases for ncu captures only)")
     ap.add_argument("--seq", type=int, default=None,
@@ -84,6 +94,10 @@ def parse_args():
                     help="force the per-op kernel chain instead of the fused kernel")
     ap.add_argument("--e2e-chunks", type=int, default=None,
                     help="sub-batches per e2e step (default: host transfers of 128-256 MB, at most 8)")
+    ap.add_argument("--per-config", default="c1,c3,c4,c5",
+                    help="comma list of further configs measured into per_config ('' for none)")
+    ap.add_argument("--accuracy-seqs", type=int, default=256,
+                    help="sequences of the headline output checked against the oracle")
     ap.add_argument("--decode", type=int, default=None, metavar="CACHE_LEN",
                     help="time KV-cached decoding instead: one new token per sequence over a "
                          "cache of CACHE_LEN tokens (the config's geometry)")
@@ -199,11 +213,18 @@ class ClockSampler:
                 "samples": len(rows)}
 
 
-def make_input(B, S, D, seed):
+def make_shard(start, stop, S, D, seed, dev):
+    """Sequences [start, stop) of a config's input: sequence b is N(0,1) from
+    its own generator seeded seed + b, so a shard does not depend on how the
+    batch is split. Long sequences are drawn on the device."""
     import torch
 
-    g = torch.Generator().manual_seed(seed)
-    return torch.randn(B, S, D, generator=g)
+    on_dev = S * D >= (1 << 22)
+    out = torch.empty(stop - start, S, D, device=dev if on_dev else "cpu")
+    for i, b in enumerate(range(start, stop)):
+        g = torch.Generator(device=dev if on_dev else "cpu").manual_seed(seed + b)
+        out[i] = torch.randn(S, D, generator=g, device=out.device)
+    return out
 
 
 def cpu_sample(name):
@@ -268,7 +289,7 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": f"{args.config} (CPU sample)", "sample": sample},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(),
                          "kind": "port", "sample": sample},
@@ -473,6 +494,249 @@ def run_decode(args):
     return 0
 
 
+
+
+# Timed steps and the oracle sample per config when it is not the headline
+# (bounded timed work: c1/c4 ~0.1 ms, c3 ~0.7 ms, c5 ~1.8 s per forward).
+PER_CONFIG_STEPS = {"c1": 200, "c2": 50, "c3": 100, "c4": 200, "c5": 2}
+ACCURACY_SEQS = {"c1": 4, "c2": 256, "c3": 8, "c4": 16, "c5": 1}
+C5_PREFIX = 2048  # c5 accuracy: causal prefix rows (exact for a causal model)
+
+
+class Ranks:
+    """Barrier / max-over-ranks / clock sampling for one process per GPU."""
+
+    def __init__(self, torch, dist, rank, local_rank, world, dev):
+        self.torch, self.dist = torch, dist
+        self.rank, self.local_rank, self.world, self.dev = rank, local_rank, world, dev
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+        self.torch.cuda.synchronize()
+
+    def max(self, v):
+        if self.world == 1:
+            return v
+        t = self.torch.tensor([v], device=self.dev, dtype=self.torch.float64)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sampler(self):
+        return ClockSampler(smi_gpu_id(self.local_rank)) if self.local_rank == 0 else None
+
+
+def accuracy_sample(model, y, start, S, D, H, F, L, n_seq, seed, name):
+    """Seeded sample of this rank's output rows against the FP32 oracle on
+    the same weights and inputs (the reference's rule: |d| <= 0.002 or
+    |d| <= 0.02 |ref|); c5 compares the first C5_PREFIX rows, which a causal
+    model computes from the prefix alone."""
+    import torch
+    from oracle import baseline as ob
+
+    n_local = y.shape[0]
+    n = min(n_seq, n_local)
+    idx = torch.randperm(n_local, generator=torch.Generator().manual_seed(seed))[:n].sort().values
+    rows = min(S, C5_PREFIX) if S > 4096 else S
+    xs = torch.stack([make_shard(start + int(i), start + int(i) + 1, S, D, SEED + 100000,
+                                 y.device)[0, :rows].cpu() for i in idx])
+    cfg = ob.TransformerConfig(n, rows, D, H, F, L, True)
+    ref_model = ob.BaselineTransformer(cfg).eval()
+    ref_model.load_state_dict({k: v.detach().cpu() for k, v in model.state_dict().items()})
+    with torch.inference_mode():
+        ref = ref_model(xs)
+    got = y[idx.to(y.device), :rows].float().cpu()
+    res = ob.compare_outputs(ref, got, rtol=0.02, atol=0.002)
+    return {"failed_elements": res.failed_elements, "total_elements": res.total_elements,
+            "max_abs": res.max_abs_error,
+            "sample": f"{n} seeded sequences of rank 0's shard" +
+                      (f", first {rows} rows (causal prefix)" if rows < S else "") +
+                      ", FP32 oracle on the host, rule |d|<=0.002 or |d|<=0.02|ref|"}
+
+
+def measure(pkg, R, name, args, headline):
+    """Time one config's forward on this rank's shard of its global batch.
+    Collectives (barriers, max over ranks, the final gather) run on every
+    rank in the same order, including ranks whose shard is empty."""
+    import torch
+
+    Bg, S, D, H, F, L = CONFIGS[name]
+    if headline and args.batch:
+        Bg = args.batch
+    if headline and args.seq:
+        S = args.seq
+    start, stop = pkg.sharding.shard_range(Bg, R.world, R.rank)
+    B = stop - start
+    steps = args.steps if headline else PER_CONFIG_STEPS[name]
+    warmup = max(3, args.warmup)
+    torch.manual_seed(SEED)
+    model = pkg.UserOptimizedTransformer(pkg.TransformerConfig(Bg, S, D, H, F, L, True))
+    model = model.to(R.dev).eval()
+    model.enable_fused_forward(not args.chain)
+    lib = pkg._lib.load()
+    mdl = model._prepare(R.dev)[3]
+    fused = B > 0 and lib.tfx_forward_workspace_bytes(ctypes.byref(mdl), B, S) == 0
+    x = make_shard(start, stop, S, D, SEED + 100000, R.dev)
+    x_host = x if not x.is_cuda else None
+    x = x.to(R.dev)
+    y = torch.empty_like(x)
+    out = {}
+
+    # ---- value: whole-forward graph replays, input resident in HBM
+    with torch.inference_mode():
+        fg = pkg.ForwardGraph(model, x, y) if B > 0 else None
+        for _ in range(warmup):
+            if fg:
+                fg.replay()
+        sampler = R.sampler()
+        if sampler:
+            sampler.start()
+        R.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            if fg:
+                fg.replay()
+        e1.record()
+        R.barrier()
+        clocks = sampler.stop() if sampler else None
+        ms_total = R.max(e0.elapsed_time(e1))
+    ms = ms_total / steps
+    tokens = Bg * S
+    value = tokens / (ms / 1e3)
+    vt_path = (D // H) in (64, 128)
+    launches = 1 if fused else (8 if vt_path else 7) * L + 1
+
+    # ---- e2e: public API with host buffers (not c5: 13 GB each way)
+    e2e = None
+    if not args.no_e2e and S <= 4096:
+        if x_host is None:
+            x_host = x.cpu()
+        x_pin = x_host.pin_memory()
+        y_pin = torch.empty_like(x_pin).pin_memory()
+        e2e_steps = max(3, min(steps, 40))  # pipeline fill and drain: ~3 % of the run
+        chunks = args.e2e_chunks or max(1, min(8, x_pin.numel() * 4 // (128 << 20)))
+        while B > 0 and B % chunks:
+            chunks -= 1
+        bc = max(1, B // chunks)
+        xs = [x_pin[i * bc:(i + 1) * bc] for i in range(chunks)]
+        ys = [y_pin[i * bc:(i + 1) * bc] for i in range(chunks)]
+        # One CUDA Graph of the three-stream pipeline (StreamingForward.capture)
+        # covers e2e_steps steps, copies included; median of three replays.
+        with torch.inference_mode():
+            pipe = None
+            if B > 0:
+                sf = pkg.StreamingForward(model, R.dev, bc, S)
+                sf.run(xs, ys)
+                torch.cuda.synchronize()
+                pipe = sf.capture(xs * e2e_steps, ys * e2e_steps)
+                pipe.replay()
+                torch.cuda.synchronize()
+            reps = []
+            for _ in range(3):
+                R.barrier()
+                a = torch.cuda.Event(enable_timing=True)
+                b = torch.cuda.Event(enable_timing=True)
+                a.record()
+                if pipe:
+                    pipe.replay()
+                b.record()
+                torch.cuda.synchronize()
+                R.barrier()
+                reps.append(R.max(a.elapsed_time(b)) / e2e_steps)
+            e2e_ms = statistics.median(reps)
+            del pipe
+        e2e = {"value": tokens / (e2e_ms / 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": Bg * S * D * 4, "d2h_bytes_per_step": Bg * S * D * 4,
+               "ms_per_step": e2e_ms,
+               "pipeline": f"upload / forward / download overlapped on three streams per rank, "
+                           f"{chunks} sub-batch(es) of {bc} sequences per rank step, "
+                           f"{e2e_steps} steps per CUDA Graph replay"}
+
+    # ---- roofline of the dominant kernel (this rank's launches)
+    hbm, tf_burst, tf_sust, peak_kind = load_peaks()
+    M = B * S
+    roof, share = None, None
+    if B > 0:
+        if fused:
+            dom = "fused_forward"
+            per = {dom: [ms]}
+            nbytes = M * D * 8 + L * (4 * D * D + 2 * D * F) * 2
+            nflops = flops_per_token(S, D, H, F, L) * M
+        else:
+            with torch.inference_mode():
+                ws = model._workspace_for(R.dev, mdl, B, S)
+                per = kernel_breakdown(pkg, model, x, ws, steps=max(2, min(steps, 10)))
+            totals = {k: sum(v) for k, v in per.items()}
+            dom = max(totals, key=totals.get)
+            nbytes, nflops = algorithmic(dom, M, S, D, H, F)
+        totals = {k: sum(v) for k, v in per.items()}
+        share = {k: round(v / sum(totals.values()), 4) for k, v in totals.items()}
+        mean_ms = statistics.mean(per[dom])
+        traffic = load_traffic().get((dom, name))
+        if nflops / max(nbytes, 1) < (tf_burst * 1e12) / (hbm * 1e9):
+            achieved = nbytes / (mean_ms / 1e3) / 1e9
+            roof = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                    "frac": achieved / hbm, "traffic": traffic, "kernel": dom,
+                    "algorithmic_bytes_per_launch": nbytes, "mean_launch_ms": mean_ms,
+                    "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"}
+        else:
+            achieved = nflops / (mean_ms / 1e3) / 1e12
+            # Burst peak at full clock; the sustained (power-capped) peak when
+            # the cap held the SM clock below its maximum in the timed region.
+            capped = (bool(clocks) and "sw_power_cap" in (clocks.get("reasons") or []) and tf_sust
+                      and (clocks.get("sm_mhz") or 0) < 0.97 * (clocks.get("sm_max_mhz") or 1e9))
+            tf = tf_sust if capped else tf_burst
+            roof = {"bound": "tensor", "achieved": achieved, "peak": tf, "unit": "TFLOP/s",
+                    "frac": achieved / tf, "traffic": traffic, "kernel": dom,
+                    "algorithmic_flops_per_launch": nflops, "algorithmic_bytes_per_launch": nbytes,
+                    "mean_launch_ms": mean_ms,
+                    "peak_source": f"{peak_kind} (MEASURED_PEAKS.json "
+                                   f"{'bf16_tflops_sustained: sw_power_cap active' if capped else 'bf16_tflops'})"}
+        if fg:
+            fg.replay()  # y = forward(x) for the accuracy check and the gather
+        torch.cuda.synchronize()
+
+    # ---- final gather of the outputs to rank 0 (outside the timed region)
+    gather_ms = None
+    if R.world > 1:
+        with torch.inference_mode():
+            R.barrier()
+            t0 = time.perf_counter()
+            full = pkg.sharding.gather_shards(y, Bg, dst=0)
+            torch.cuda.synchronize()
+            gather_ms = (time.perf_counter() - t0) * 1e3
+            del full
+
+    acc = None
+    if R.rank == 0 and B > 0 and not args.no_accuracy:
+        acc = accuracy_sample(model, y, start, S, D, H, F, L,
+                              args.accuracy_seqs if headline else ACCURACY_SEQS[name],
+                              SEED + 7, name)
+
+    out = {
+        "value": value, "unit": UNIT, "ms_per_step": ms, "steps": steps, "warmup": warmup,
+        "fwd_tflops_algorithmic": flops_per_token(S, D, H, F, L) * tokens / (ms / 1e3) / 1e12,
+        "config": {
+            "workload": f"{name}: global B={Bg} S={S} D={D} H={H} F={F} L={L} causal "
+                        "pre-norm Transformer forward",
+            "global_batch": Bg, "seq_len": S,
+            "parallelism": f"batch shards x{R.world} ({B} sequences on rank {R.rank})",
+            "path": "fused whole-forward kernel" if fused else "per-op kernel chain",
+        },
+        "roofline": roof, "kernel_share": share, "e2e": e2e, "accuracy": acc,
+        "gpu_launches": steps * launches if B > 0 else 0, "clocks": clocks,
+        "vs_baseline": value / REFERENCE_PUBLISHED[name] if name in REFERENCE_PUBLISHED else None,
+    }
+    if gather_ms is not None:
+        out["final_gather_ms"] = gather_ms
+        out["final_gather_bytes"] = Bg * S * D * 4
+    del fg, model, x, y
+    torch.cuda.empty_cache()
+    return out
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
@@ -492,210 +756,55 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=dev)
     pkg = importlib.import_module("gpu-kernel-for-transformer_b200")
-    lib = pkg._lib.load()
+    R = Ranks(torch, dist, rank, local_rank, world, dev)
 
-    B, S, D, H, F, L = CONFIGS[args.config]
-    if args.batch:
-        B = args.batch
-    if args.seq:
-        S = args.seq
-    cfg = pkg.TransformerConfig(B, S, D, H, F, L, True)
-    torch.manual_seed(SEED)
-    model = pkg.UserOptimizedTransformer(cfg).to(dev).eval()
-    model.enable_fused_forward(not args.chain)
-    x_host = make_input(B, S, D, SEED + 100000 + rank)
-    x = x_host.to(dev)
-    y = torch.empty_like(x)
-    mdl = model._prepare(dev)[3]
-    fused = lib.tfx_forward_workspace_bytes(ctypes.byref(mdl), B, S) == 0
+    head = measure(pkg, R, args.config, args, headline=True)
+    per_config = {}
+    for name in [c for c in args.per_config.split(",") if c and c != args.config]:
+        per_config[name] = measure(pkg, R, name, args, headline=False)
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    def max_over_ranks(v):
-        if world == 1:
-            return v
-        t = torch.tensor([v], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    # ---- value: whole-forward graph replays, input resident in HBM
-    with torch.inference_mode():
-        fg = pkg.ForwardGraph(model, x, y)
-        for _ in range(max(3, args.warmup)):
-            fg.replay()
-        sampler = ClockSampler(smi_gpu_id(local_rank)) if local_rank == 0 else None
-        if sampler:
-            sampler.start()
-        barrier()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(args.steps):
-            fg.replay()
-        e1.record()
-        barrier()
-        clocks = sampler.stop() if sampler else None
-        ms_total = max_over_ranks(e0.elapsed_time(e1))
-    ms_per_step = ms_total / args.steps
-    tokens_per_step = world * B * S
-    value = tokens_per_step / (ms_per_step / 1e3)
-    # Per-op chain: LN, then per layer QKV GEMM, [V transpose,] attention,
-    # out-proj, LN, FFN-in, FFN-out, LN.
-    vt_path = (D // H) in (64, 128)
-    launches_per_forward = 1 if fused else (8 if vt_path else 7) * L + 1
-
-    # ---- e2e: public API with host buffers. Every step uploads its input
-    # from pinned host memory, runs the forward and downloads the output; the
-    # package's StreamingForward overlaps the download of one sub-batch, the
-    # forward of the next and the upload of the one after on three streams
-    # (PCIe is full duplex). A step's B sequences go through as `chunks`
-    # sub-batches of 128-256 MB (sequences are independent), so the pipeline's
-    # fill and drain are a fraction of a step (c2: 4 sub-batches 91.9 -> 94.8 M
-    # tokens/s; pinned copies on the box run 50 GB/s per direction in duplex,
-    # a 13.1 ms floor per step). The timed region spans the first upload to the
-    # last download.
-    e2e = None
-    if not args.no_e2e:
-        x_pin = x_host.pin_memory()
-        y_pin = torch.empty_like(x_pin).pin_memory()
-        e2e_steps = max(3, min(args.steps, 40))  # pipeline fill and drain: ~3 % of 20 steps
-        chunks = args.e2e_chunks or max(1, min(8, x_pin.numel() * 4 // (128 << 20)))
-        while B % chunks:
-            chunks -= 1
-        bc = B // chunks
-        xs = [x_pin[i * bc:(i + 1) * bc] for i in range(chunks)]
-        ys = [y_pin[i * bc:(i + 1) * bc] for i in range(chunks)]
-        # The run is captured once as a CUDA Graph (StreamingForward.capture:
-        # the same three-stream pipeline with no per-step host work) and
-        # replayed; a replay covers e2e_steps steps, copies included. The
-        # median of three timed replays (host links are shared on the box).
-        with torch.inference_mode():
-            sf = pkg.StreamingForward(model, dev, bc, S)
-            sf.run(xs, ys)
-            torch.cuda.synchronize()
-            pipe = sf.capture(xs * e2e_steps, ys * e2e_steps)
-            pipe.replay()
-            torch.cuda.synchronize()
-            reps = []
-            for _ in range(3):
-                barrier()
-                a = torch.cuda.Event(enable_timing=True)
-                b = torch.cuda.Event(enable_timing=True)
-                a.record()
-                pipe.replay()
-                b.record()
-                torch.cuda.synchronize()
-                barrier()
-                reps.append(max_over_ranks(a.elapsed_time(b)) / e2e_steps)
-            e2e_ms = statistics.median(reps)
-            del pipe, sf
-        e2e = {"value": tokens_per_step / (e2e_ms / 1e3), "unit": UNIT,
-               "h2d_bytes_per_step": x_pin.numel() * 4, "d2h_bytes_per_step": y_pin.numel() * 4,
-               "ms_per_step": e2e_ms,
-               "pipeline": f"upload / forward / download overlapped on three streams, "
-                           f"{chunks} sub-batch(es) of {bc} sequences per step, "
-                           f"{e2e_steps} steps per CUDA Graph replay"}
-
-    # ---- roofline of the dominant kernel
-    hbm, tf_burst, tf_sust, peak_kind = load_peaks()
-    M = B * S
-    if fused:
-        # One kernel per forward: the timed graph replays are its launches.
-        dom = "fused_forward"
-        per = {dom: [ms_per_step]}
-        nbytes = M * D * 8 + L * (4 * D * D + 2 * D * F) * 2
-        nflops = flops_per_token(S, D, H, F, L) * M
-    else:
-        with torch.inference_mode():
-            ws = model._workspace_for(dev, mdl, B, S)
-            per = kernel_breakdown(pkg, model, x, ws, steps=max(2, min(args.steps, 10)))
-        totals = {k: sum(v) for k, v in per.items()}
-        dom = max(totals, key=totals.get)
-        nbytes, nflops = algorithmic(dom, M, S, D, H, F)
-    totals = {k: sum(v) for k, v in per.items()}
-    share = {k: round(v / sum(totals.values()), 4) for k, v in totals.items()}
-    mean_ms = statistics.mean(per[dom])
-    traffic = load_traffic().get((dom, args.config))
-    # Bound = the roof this kernel meets first at the measured peaks.
-    if nflops / max(nbytes, 1) < (tf_burst * 1e12) / (hbm * 1e9):
-        achieved = nbytes / (mean_ms / 1e3) / 1e9
-        roof = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                "frac": achieved / hbm, "traffic": traffic, "kernel": dom,
-                "algorithmic_bytes_per_launch": nbytes, "mean_launch_ms": mean_ms,
-                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"}
-    else:
-        achieved = nflops / (mean_ms / 1e3) / 1e12
-        # Burst peak for a kernel that runs at full clock; the sustained
-        # (power-capped) peak when the power cap held the SM clock below its
-        # maximum while this workload was timed (long tensor-bound steps such
-        # as c5's; a cap flag at full clock leaves the burst peak).
-        capped = (bool(clocks) and "sw_power_cap" in (clocks.get("reasons") or []) and tf_sust
-                  and (clocks.get("sm_mhz") or 0) < 0.97 * (clocks.get("sm_max_mhz") or 1e9))
-        tf = tf_sust if capped else tf_burst
-        roof = {"bound": "tensor", "achieved": achieved, "peak": tf, "unit": "TFLOP/s",
-                "frac": achieved / tf, "traffic": traffic, "kernel": dom,
-                "algorithmic_flops_per_launch": nflops, "algorithmic_bytes_per_launch": nbytes,
-                "mean_launch_ms": mean_ms,
-                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json "
-                               f"{'bf16_tflops_sustained: sw_power_cap active' if capped else 'bf16_tflops'})"}
-
-    # ---- final gather of outputs to rank 0 (outside the timed region)
-    gather_ms = None
-    if world > 1:
-        with torch.inference_mode():
-            fg.replay()
-            barrier()
-            t0 = time.perf_counter()
-            full = pkg.sharding.gather_shards(y, world * B, dst=0)
-            torch.cuda.synchronize()
-            gather_ms = (time.perf_counter() - t0) * 1e3
-            del full
-
-    fwd_flops = flops_per_token(S, D, H, F, L) * tokens_per_step
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(args.config, args.cpu_seconds)
 
     if rank == 0:
+        cfg = head["config"]
+        cfg.update({
+            "l2": "input and output per GPU larger than L2 (126 MB) for c2; no flush",
+            "compute": "fp16 tensor-core operands, fp32 accumulate/residual/LayerNorm",
+            "vs_baseline_basis": "reference optimized path on RTX 3060 Laptop "
+                                 "(README.md:180-191), same shape",
+            "tflops_algorithmic": head["fwd_tflops_algorithmic"],
+            "input": "sequence b ~ N(0,1) from seed 101234+b; seeded default-init weights",
+        })
         line = {
             "metric": METRIC,
-            "value": value,
+            "value": head["value"],
             "unit": UNIT,
             "n_gpus": world,
-            "steps": args.steps,
-            "warmup": args.warmup,
-            "ms_per_step": ms_per_step,
+            "steps": head["steps"],
+            "warmup": head["warmup"],
+            "ms_per_step": head["ms_per_step"],
             "higher_is_better": True,
-            "scaling": "weak",
-            "vs_baseline": value / REFERENCE_PUBLISHED[args.config],
+            "scaling": "strong",
+            "vs_baseline": head["vs_baseline"],
             "dtype": "fp16",
             "data": "synthetic",
-            "config": {
-                "workload": f"{args.config}: B={B}/GPU S={S} D={D} H={H} F={F} L={L} causal "
-                            "pre-norm Transformer forward",
-                "global_batch": B * world, "seq_len": S, "parallelism": f"batch shards x{world}",
-                "path": "fused whole-forward kernel" if fused else "per-op kernel chain",
-                "l2": "input and output per GPU larger than L2 (126 MB); no flush",
-                "compute": "fp16 tensor-core operands, fp32 accumulate/residual/LayerNorm",
-                "vs_baseline_basis": "reference optimized path on RTX 3060 Laptop "
-                                     "(README.md:180-191), same shape",
-                "tflops_algorithmic": fwd_flops / (ms_per_step / 1e3) / 1e12,
-            },
-            "roofline": roof,
-            "kernel_share": share,
+            "config": cfg,
+            "roofline": head["roofline"],
+            "kernel_share": head["kernel_share"],
             "cpu_baseline": cpu,
-            "e2e": e2e,
-            "gpu_launches": args.steps * launches_per_forward,
-            "clocks": clocks,
+            "e2e": head["e2e"],
+            "accuracy": head["accuracy"],
+            "gpu_launches": head["gpu_launches"],
+            "clocks": head["clocks"],
+            "per_config": per_config,
         }
-        if gather_ms is not None:
-            line["final_gather_ms"] = gather_ms
+        for k in ("final_gather_ms", "final_gather_bytes"):
+            if k in head:
+                line[k] = head[k]
         print(json.dumps(line))
 
-    del fg
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

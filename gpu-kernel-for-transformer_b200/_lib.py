@@ -29,6 +29,12 @@ TFX_ERR_DEVICE = -6
 TFX_DTYPE_F16 = 0
 TFX_DTYPE_F32 = 1
 
+TFX_DEV_TIMEOUT_FULL = 1
+TFX_DEV_TIMEOUT_EMPTY = 2
+TFX_DEV_TIMEOUT_ACCUM = 3
+TFX_DEV_TIMEOUT_ACCUM_FREE = 4
+TFX_DEV_TIMEOUT_OTHER = 5
+
 TFX_PATH_AUTO = 0
 TFX_PATH_CHAIN = 1
 
@@ -58,6 +64,7 @@ SIGNATURES = {
     "tfx_forward_kv_workspace_bytes": (_I64, [_P, _I, _I]),
     "tfx_forward_kv": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _P, _P, ctypes.c_size_t, _P]),
     "tfx_read_device_error": (_I, [ctypes.POINTER(_I)]),
+    "tfx_selftest_bounded_wait": (_I, [_I64, _P]),
 }
 
 

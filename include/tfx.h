@@ -246,6 +246,29 @@ TFX_API int tfx_forward_kv(const tfx_model* model, const float* x, float* y, int
  */
 TFX_API int tfx_read_device_error(int* code);
 
+/*
+ * Error codes a kernel writes to the device error word (first one wins).
+ */
+enum {
+  TFX_DEV_TIMEOUT_FULL = 1,       /* gave up waiting for a loaded stage          */
+  TFX_DEV_TIMEOUT_EMPTY = 2,      /* producer gave up waiting for a free stage   */
+  TFX_DEV_TIMEOUT_ACCUM = 3,      /* gave up waiting for an accumulator          */
+  TFX_DEV_TIMEOUT_ACCUM_FREE = 4, /* gave up waiting for a free accumulator      */
+  TFX_DEV_TIMEOUT_OTHER = 5
+};
+
+/*
+ * Runs the bounded-wait protocol of the pipelined kernels on a wait that
+ * cannot complete: one CTA holds a TMEM allocation and a bulk copy in
+ * flight while a consumer warp waits on an mbarrier nobody arrives on, for
+ * at most limit_cycles SM cycles (0 < limit_cycles <= 2e9, about 1 s); it then
+ * records TFX_DEV_TIMEOUT_ACCUM, drains its copy, frees TMEM and returns.
+ * tfx_read_device_error afterwards reports the code and the context stays
+ * usable. For tests of failure detection. No reference counterpart (the
+ * reference's kernels have no waits).
+ */
+TFX_API int tfx_selftest_bounded_wait(int64_t limit_cycles, tfx_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -270,3 +270,18 @@ def blockwise_causal_attention_fp64(q, k, v, scale, block=1024):
         p = torch.softmax(sc, dim=-1)
         out[q0:q1] = p @ v[:q1]
     return out
+
+
+def causal_attention_rows_fp64(q, k, v, rows, scale):
+    """Selected query rows of causal softmax(Q.K^T*scale).V in float64.
+
+    q, k, v are [S, hd] for one (batch, head); ``rows`` lists query positions;
+    row r attends keys 0..r (torch_transformer_benchmark.py:237-253). Returns
+    [len(rows), hd] float64. For spot checks of late rows of very long
+    sequences, where even the blockwise full computation is too slow.
+    """
+    rows = torch.as_tensor(rows, dtype=torch.long)
+    hi = int(rows.max()) + 1
+    sc = (q[rows].double() @ k[:hi].double().T) * scale
+    sc = sc.masked_fill(torch.arange(hi)[None, :] > rows[:, None], -math.inf)
+    return torch.softmax(sc, dim=-1) @ v[:hi].double()

@@ -226,3 +226,11 @@ def test_kv_forward_validates_on_the_host(lib):
     assert call(model=nc) == L.TFX_ERR_UNSUPPORTED
     assert b"causal" in lib.tfx_last_error_message()
     assert lib.tfx_forward_kv_workspace_bytes(ctypes.byref(m), 0, 3) == -1
+
+
+def test_selftest_limit_is_checked_on_the_host(lib):
+    pkg = load_package()
+    L = pkg._lib
+    assert lib.tfx_selftest_bounded_wait(0, None) == L.TFX_ERR_INVALID_ARGUMENT
+    assert lib.tfx_selftest_bounded_wait(3_000_000_000, None) == L.TFX_ERR_INVALID_ARGUMENT
+    assert b"limit_cycles" in lib.tfx_last_error_message()

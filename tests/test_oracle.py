@@ -81,3 +81,14 @@ def test_blockwise_attention_matches_explicit():
     sc = sc.masked_fill(torch.ones(300, 300, dtype=torch.bool).triu(1), float("-inf"))
     ref = torch.softmax(sc, -1) @ v.double()
     assert torch.allclose(out, ref, atol=1e-12)
+
+
+def test_rows_attention_oracle_equals_blockwise():
+    """causal_attention_rows_fp64 (late-row spot checks) agrees with the
+    blockwise float64 attention on every row it is asked for."""
+    g = torch.Generator().manual_seed(0)
+    q, k, v = (torch.randn(300, 16, generator=g) for _ in range(3))
+    full = ob.blockwise_causal_attention_fp64(q, k, v, 0.25, block=64)
+    rows = torch.tensor([0, 5, 150, 299])
+    assert torch.allclose(ob.causal_attention_rows_fp64(q, k, v, rows, 0.25), full[rows],
+                          atol=1e-12, rtol=0)
