@@ -55,11 +55,13 @@ SIGNATURES = {
     "tfx_residual_layer_norm": (_I, [_P, _P, _P, _P, _P, _P, _I, _I64, _I, _F, _I, _P]),
     "tfx_linear": (_I, [_P, _P, _P, _P, _P, _I64, _I, _I, _I, _P]),
     "tfx_attention": (_I, [_P, _P, _P, _I64, _P, _I64, _I, _I, _I, _I, _F, _I, _P, _P]),
+    "tfx_attention_masked": (_I, [_P, _P, _P, _I64, _P, _I64, _I, _I, _I, _I, _F, _I, _P, _P]),
     "tfx_attention_vt_ld": (_I64, [_I]),
     "tfx_transpose_v": (_I, [_P, _I64, _P, _I, _I, _I, _P]),
     "tfx_attention_vt": (_I, [_P, _P, _P, _I64, _P, _I64, _I, _I, _I, _I, _F, _I, _P, _P]),
     "tfx_forward_workspace_bytes": (_I64, [_P, _I, _I]),
     "tfx_forward": (_I, [_P, _P, _P, _I, _I, _P, _P, ctypes.c_size_t, _P]),
+    "tfx_forward_masked": (_I, [_P, _P, _P, _I, _I, _P, _P, ctypes.c_size_t, _P]),
     "tfx_forward_static": (_I, [_P, _P, _P, _I, _I, _P, _P]),
     "tfx_forward_kv_workspace_bytes": (_I64, [_P, _I, _I]),
     "tfx_forward_kv": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _P, _P, ctypes.c_size_t, _P]),

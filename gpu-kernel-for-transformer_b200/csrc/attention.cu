@@ -7,6 +7,7 @@
 // never materialised. Scores are computed in the log2 domain
 // (scale * log2(e) folded in) and exponentiated with exp2f.
 //
+// Key padding: prefix lengths (valid_len) or a key bitmask of any pattern.
 // Head dims 8 and 16 pad the QK^T reduction to the 16-wide MMA K: the pad
 // columns of the Q and K tiles are zero-filled once, so they add nothing.
 // Causal CTAs are launched heaviest-first (last query block first).
@@ -77,7 +78,8 @@ __global__ void __launch_bounds__(kAttnThreads)
     attention_mma_kernel(const __half* __restrict__ q, int64_t ld_q, const __half* __restrict__ k,
                          const __half* __restrict__ v, AttnKv kv, __half* __restrict__ out,
                          int64_t ld_out, int heads, int q_len, float scale_log2,
-                         const int32_t* __restrict__ valid_len) {
+                         const int32_t* __restrict__ valid_len,
+                         const uint32_t* __restrict__ key_bits, int key_words) {
   grid_dep_wait();
   grid_dep_launch();
   using C = AttnCfg<HD>;
@@ -171,8 +173,19 @@ __global__ void __launch_bounds__(kAttnThreads)
     }
     // ---- mask + online softmax (log2 domain)
     const int k0 = kb * BKV;
-    const bool need_mask =
-        (k0 + BKV > kend) || (CAUSAL && k0 + BKV - 1 > kv.q_off + q0 + warp * 16);
+    // Key bitmask (any padding pattern): the BKV bits of this tile, the
+    // same for every row (uniform loads).
+    uint32_t kw[BKV / 32];
+    bool bits_full = true;
+#pragma unroll
+    for (int w = 0; w < BKV / 32; ++w) {
+      const int wi = k0 / 32 + w;
+      kw[w] = (key_bits == nullptr) ? 0xffffffffu
+              : (wi < key_words ? key_bits[static_cast<int64_t>(b) * key_words + wi] : 0u);
+      bits_full = bits_full && kw[w] == 0xffffffffu;
+    }
+    const bool need_mask = !bits_full || (k0 + BKV > kend) ||
+                           (CAUSAL && k0 + BKV - 1 > kv.q_off + q0 + warp * 16);
     float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
     for (int j = 0; j < NT_S; ++j) {
@@ -180,9 +193,11 @@ __global__ void __launch_bounds__(kAttnThreads)
       for (int e = 0; e < 4; ++e) {
         float val = s[j][e] * scale_log2;
         if (need_mask) {
-          const int key = k0 + j * 8 + 2 * t + (e & 1);
+          const int kk = j * 8 + 2 * t + (e & 1);  // key within the tile
+          const int key = k0 + kk;
           const int qr = qpos_a + (e >> 1) * 8;
-          if (key >= kend || (CAUSAL && key > qr)) val = -INFINITY;
+          if (key >= kend || (CAUSAL && key > qr) || !((kw[kk >> 5] >> (kk & 31)) & 1u))
+            val = -INFINITY;
         }
         s[j][e] = val;
         mx[e >> 1] = fmaxf(mx[e >> 1], val);
@@ -270,7 +285,7 @@ __global__ void __launch_bounds__(kAttnThreads)
 template <int HD>
 int launch_hd(const __half* q, int64_t ld_q, const __half* k, const __half* v, const AttnKv& kv,
               __half* out, int64_t ld_out, int batch, int heads, int q_len, float scale,
-              int causal, const int32_t* valid_len, cudaStream_t stream) {
+              int causal, const KeyMask& km, cudaStream_t stream) {
   using C = AttnCfg<HD>;
   static int done_c[kMaxDevices] = {0};
   static int done_n[kMaxDevices] = {0};
@@ -281,39 +296,39 @@ int launch_hd(const __half* q, int64_t ld_q, const __half* k, const __half* v, c
     int st = ensure_smem(reinterpret_cast<const void*>(kern), C::kSmemBytes, done_c);
     if (st != TFX_OK) return st;
     launch_pdl(kern, grid, dim3(kAttnThreads), C::kSmemBytes, stream, q, ld_q, k, v, kv, out,
-               ld_out, heads, q_len, scale_log2, valid_len);
+               ld_out, heads, q_len, scale_log2, km.len, km.bits, key_words(kv.len));
   } else {
     auto kern = attention_mma_kernel<HD, false>;
     int st = ensure_smem(reinterpret_cast<const void*>(kern), C::kSmemBytes, done_n);
     if (st != TFX_OK) return st;
     launch_pdl(kern, grid, dim3(kAttnThreads), C::kSmemBytes, stream, q, ld_q, k, v, kv, out,
-               ld_out, heads, q_len, scale_log2, valid_len);
+               ld_out, heads, q_len, scale_log2, km.len, km.bits, key_words(kv.len));
   }
   return check_launch("attention_mma_kernel");
 }
 
 int launch_mma(const __half* q, int64_t ld_q, const __half* k, const __half* v, const AttnKv& kv,
                __half* out, int64_t ld_out, int batch, int heads, int q_len, int head_dim,
-               float scale, int causal, const int32_t* valid_len, cudaStream_t stream) {
+               float scale, int causal, const KeyMask& km, cudaStream_t stream) {
   switch (head_dim) {
     case 8:
       return launch_hd<8>(q, ld_q, k, v, kv, out, ld_out, batch, heads, q_len, scale, causal,
-                          valid_len, stream);
+                          km, stream);
     case 16:
       return launch_hd<16>(q, ld_q, k, v, kv, out, ld_out, batch, heads, q_len, scale, causal,
-                           valid_len, stream);
+                           km, stream);
     case 32:
       return launch_hd<32>(q, ld_q, k, v, kv, out, ld_out, batch, heads, q_len, scale, causal,
-                           valid_len, stream);
+                           km, stream);
     case 64:
       return launch_hd<64>(q, ld_q, k, v, kv, out, ld_out, batch, heads, q_len, scale, causal,
-                           valid_len, stream);
+                           km, stream);
     case 128:
       return launch_hd<128>(q, ld_q, k, v, kv, out, ld_out, batch, heads, q_len, scale, causal,
-                            valid_len, stream);
+                            km, stream);
     case 256:
       return launch_hd<256>(q, ld_q, k, v, kv, out, ld_out, batch, heads, q_len, scale, causal,
-                            valid_len, stream);
+                            km, stream);
     default:
       return fail(TFX_ERR_UNSUPPORTED, "tfx_attention: head_dim %d not in {8,16,32,64,128,256}",
                   head_dim);
@@ -634,13 +649,13 @@ int launch_decode_hd(const __half* q, int64_t ld_q, const __half* k, const __hal
 
 int launch_attention(const __half* q, const __half* k, const __half* v, int64_t ld_qkv,
                      __half* out, int64_t ld_out, int batch, int heads, int seq, int head_dim,
-                     float scale, int causal, const int32_t* valid_len, cudaStream_t stream) {
+                     float scale, int causal, const KeyMask& km, cudaStream_t stream) {
   // Head dims 64, 128 and 256 run on the tcgen05 kernel (attention_tc.cu).
   if (attention_tc_supported(head_dim, scale))
     return launch_attention_tc(q, k, v, ld_qkv, out, ld_out, batch, heads, seq, head_dim, scale,
-                               causal, valid_len, stream);
+                               causal, km, stream);
   return launch_mma(q, ld_qkv, k, v, AttnKv{ld_qkv, seq, seq, 0}, out, ld_out, batch, heads, seq,
-                    head_dim, scale, causal, valid_len, stream);
+                    head_dim, scale, causal, km, stream);
 }
 
 size_t attention_decode_part_bytes(int batch, int heads, int q_len, int head_dim) {
@@ -691,7 +706,7 @@ int launch_attention_kv(const __half* q, int64_t ld_q, const __half* k, const __
     return launch_attention_tc_kv(q, ld_q, k, v, kv, out, ld_out, batch, heads, q_len, head_dim,
                                   scale, stream);
   return launch_mma(q, ld_q, k, v, kv, out, ld_out, batch, heads, q_len, head_dim, scale, 1,
-                    nullptr, stream);
+                    KeyMask{}, stream);
 }
 
 }  // namespace tfx

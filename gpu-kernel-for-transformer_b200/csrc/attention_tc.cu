@@ -39,8 +39,10 @@
 // Scores are handled in the log2 domain: c = scale * log2(e) folds the
 // softmax scale into the exponent's FMA.
 //
-// Masking: causal (key > query position) and key padding (key >=
-// valid_len[b]) apply only on a tile's diagonal / ragged KV tile. Rows past
+// Masking: causal (key > query position) and prefix key padding (key >=
+// valid_len[b]) apply only on a tile's diagonal / ragged KV tile; a key
+// bitmask (any padding pattern: bit k of word w of sequence b = key 32w+k
+// is valid) masks each KV tile whose 128 bits are not all set. Rows past
 // the sequence end are read as zeros by the 3-D tensor maps and never stored.
 // Queries may sit at an offset among the keys (new tokens over a KV cache:
 // query row i at key position q_off + i).
@@ -102,7 +104,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v, __half* __restrict__ out,
                         int64_t ld_out, int heads, int q_len, int nqb, int kv_len, int q_off,
-                        float scale_log2, const int32_t* __restrict__ valid_len, int bh_in_y,
+                        float scale_log2, const int32_t* __restrict__ valid_len,
+                        const uint32_t* __restrict__ key_bits, int key_words, int bh_in_y,
                         int* err) {
   grid_dep_wait();
   grid_dep_launch();
@@ -366,6 +369,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int c = 0; c < kTile; ++c)
           if (c >= c0) s[c] = 0xff800000u;  // -inf
       }
+      if (key_bits != nullptr) {
+        // Key padding of any pattern: bit k of the tile's 128-bit word is key
+        // j*128 + k (same for every row: uniform loads, L1 broadcast).
+        uint32_t kw[4];
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          const int wi = 4 * j + w;
+          kw[w] = wi < key_words ? key_bits[static_cast<int64_t>(b) * key_words + wi] : 0u;
+        }
+        if ((kw[0] & kw[1] & kw[2] & kw[3]) != 0xffffffffu) {
+#pragma unroll
+          for (int c = 0; c < kTile; ++c)
+            if (!((kw[c >> 5] >> (c & 31)) & 1u)) s[c] = 0xff800000u;
+        }
+      }
       float mm[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) mm[i] = fmaxf(__uint_as_float(s[i]), __uint_as_float(s[i + 8]));
@@ -518,7 +536,7 @@ __global__ void __launch_bounds__(256)
 template <int HD, bool CAUSAL, bool VT>
 int launch_tc(const __half* q, int64_t ld_q, const __half* k, const __half* v, int64_t ld_vt,
               __half* out, int64_t ld_out, int batch, int heads, int q_len, const AttnKv& kv,
-              float scale, const int32_t* valid_len, cudaStream_t stream) {
+              float scale, const KeyMask& km, cudaStream_t stream) {
   using L = TcAttn<HD>;
   static int smem_done[kMaxDevices] = {0};
   auto kern = attention_tc_kernel<HD, CAUSAL, VT>;
@@ -556,37 +574,37 @@ int launch_tc(const __half* q, int64_t ld_q, const __half* k, const __half* v, i
   const int bh_in_y = (bh <= 65535u && nqb >= 4 && kv_bytes > 256.0 * (1 << 20)) ? 1 : 0;
   const dim3 grid = bh_in_y ? dim3(static_cast<unsigned>(nqb), bh) : dim3(bh, static_cast<unsigned>(nqb));
   launch_pdl(kern, grid, dim3(kTcThreads), L::kSmem, stream, tq, tk, tv, out, ld_out, heads, q_len,
-             nqb, kv.len, kv.q_off, scale * 1.4426950408889634f, valid_len, bh_in_y,
-             device_error_word());
+             nqb, kv.len, kv.q_off, scale * 1.4426950408889634f, km.len, km.bits,
+             key_words(kv.len), bh_in_y, device_error_word());
   return check_launch("attention_tc_kernel");
 }
 
 template <int HD, bool VT>
 int launch_tc_c(const __half* q, int64_t ld_q, const __half* k, const __half* v, int64_t ld_vt,
                 __half* out, int64_t ld_out, int batch, int heads, int q_len, const AttnKv& kv,
-                float scale, int causal, const int32_t* valid_len, cudaStream_t stream) {
+                float scale, int causal, const KeyMask& km, cudaStream_t stream) {
   return causal ? launch_tc<HD, true, VT>(q, ld_q, k, v, ld_vt, out, ld_out, batch, heads, q_len,
-                                          kv, scale, valid_len, stream)
+                                          kv, scale, km, stream)
                 : launch_tc<HD, false, VT>(q, ld_q, k, v, ld_vt, out, ld_out, batch, heads, q_len,
-                                           kv, scale, valid_len, stream);
+                                           kv, scale, km, stream);
 }
 
 template <bool VT>
 int dispatch_tc(const __half* q, int64_t ld_q, const __half* k, const __half* v, int64_t ld_vt,
                 __half* out, int64_t ld_out, int batch, int heads, int q_len, const AttnKv& kv,
-                int head_dim, float scale, int causal, const int32_t* valid_len,
+                int head_dim, float scale, int causal, const KeyMask& km,
                 cudaStream_t stream) {
   if (static_cast<int64_t>(batch) * heads > 0x7fffffff || (q_len + kTile - 1) / kTile > 65535)
     return fail(TFX_ERR_UNSUPPORTED, "tfx_attention: batch*heads or seq too large for the grid");
   if (head_dim == 64)
     return launch_tc_c<64, VT>(q, ld_q, k, v, ld_vt, out, ld_out, batch, heads, q_len, kv, scale,
-                               causal, valid_len, stream);
+                               causal, km, stream);
   if (head_dim == 128)
     return launch_tc_c<128, VT>(q, ld_q, k, v, ld_vt, out, ld_out, batch, heads, q_len, kv, scale,
-                                causal, valid_len, stream);
+                                causal, km, stream);
   if (head_dim == 256)
     return launch_tc_c<256, VT>(q, ld_q, k, v, ld_vt, out, ld_out, batch, heads, q_len, kv, scale,
-                                causal, valid_len, stream);
+                                causal, km, stream);
   return fail(TFX_ERR_UNSUPPORTED, "attention_tc: head_dim %d not in {64,128,256}", head_dim);
 }
 
@@ -598,10 +616,9 @@ bool attention_tc_supported(int head_dim, float scale) {
 
 int launch_attention_tc(const __half* q, const __half* k, const __half* v, int64_t ld_qkv,
                         __half* out, int64_t ld_out, int batch, int heads, int seq, int head_dim,
-                        float scale, int causal, const int32_t* valid_len, cudaStream_t stream) {
+                        float scale, int causal, const KeyMask& km, cudaStream_t stream) {
   return dispatch_tc<false>(q, ld_qkv, k, v, 0, out, ld_out, batch, heads, seq,
-                            AttnKv{ld_qkv, seq, seq, 0}, head_dim, scale, causal, valid_len,
-                            stream);
+                            AttnKv{ld_qkv, seq, seq, 0}, head_dim, scale, causal, km, stream);
 }
 
 int64_t attention_vt_ld(int seq) { return (static_cast<int64_t>(seq) + 7) / 8 * 8; }
@@ -619,16 +636,15 @@ int launch_attention_tc_kv(const __half* q, int64_t ld_q, const __half* k, const
                            const AttnKv& kv, __half* out, int64_t ld_out, int batch, int heads,
                            int q_len, int head_dim, float scale, cudaStream_t stream) {
   return dispatch_tc<false>(q, ld_q, k, v, 0, out, ld_out, batch, heads, q_len, kv, head_dim,
-                            scale, 1, nullptr, stream);
+                            scale, 1, KeyMask{}, stream);
 }
 
 int launch_attention_tc_vt(const __half* q, const __half* k, const __half* vt, int64_t ld_qkv,
                            __half* out, int64_t ld_out, int batch, int heads, int seq,
-                           int head_dim, float scale, int causal, const int32_t* valid_len,
+                           int head_dim, float scale, int causal, const KeyMask& km,
                            cudaStream_t stream) {
   return dispatch_tc<true>(q, ld_qkv, k, vt, attention_vt_ld(seq), out, ld_out, batch, heads, seq,
-                           AttnKv{ld_qkv, seq, seq, 0}, head_dim, scale, causal, valid_len,
-                           stream);
+                           AttnKv{ld_qkv, seq, seq, 0}, head_dim, scale, causal, km, stream);
 }
 
 }  // namespace tfx

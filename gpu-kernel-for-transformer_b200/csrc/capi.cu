@@ -155,6 +155,29 @@ int check_ln_args(const char* fn, const void* x, const float* gamma, const float
   return TFX_OK;
 }
 
+int attention_checked(const char* fn, const tfx_half* q, const tfx_half* k, const tfx_half* v,
+                      int64_t ld_qkv, tfx_half* out, int64_t ld_out, int batch, int heads, int seq,
+                      int head_dim, float scale, int causal, const KeyMask& km,
+                      cudaStream_t stream) {
+  if (q == nullptr || k == nullptr || v == nullptr || out == nullptr)
+    return fail(TFX_ERR_INVALID_ARGUMENT, "%s: null tensor", fn);
+  if (batch <= 0 || heads <= 0 || seq <= 0 || head_dim <= 0)
+    return fail(TFX_ERR_INVALID_ARGUMENT, "%s: sizes must be positive", fn);
+  if (heads > 65535 || batch > 65535)
+    return fail(TFX_ERR_UNSUPPORTED, "%s: batch and heads must be <= 65535", fn);
+  if (ld_qkv < static_cast<int64_t>(heads) * head_dim ||
+      ld_out < static_cast<int64_t>(heads) * head_dim)
+    return fail(TFX_ERR_INVALID_ARGUMENT, "%s: leading dimension smaller than H*hd", fn);
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(out, 16) ||
+      ld_qkv % 8 != 0 || ld_out % 8 != 0)
+    return fail(TFX_ERR_MISALIGNED,
+                "%s: pointers 16-byte aligned and leading dims multiples of 8 needed", fn);
+  return launch_attention(reinterpret_cast<const __half*>(q), reinterpret_cast<const __half*>(k),
+                          reinterpret_cast<const __half*>(v), ld_qkv,
+                          reinterpret_cast<__half*>(out), ld_out, batch, heads, seq, head_dim,
+                          scale, causal, km, stream);
+}
+
 }  // namespace
 }  // namespace tfx
 
@@ -227,26 +250,27 @@ int tfx_linear(const tfx_half* a, const tfx_half* w, const float* bias, const fl
                        epilogue, reinterpret_cast<cudaStream_t>(stream));
 }
 
+int tfx_attention_masked(const tfx_half* q, const tfx_half* k, const tfx_half* v,
+                         int64_t ld_qkv, tfx_half* out, int64_t ld_out, int batch, int heads,
+                         int seq, int head_dim, float scale, int causal, const uint32_t* key_mask,
+                         tfx_stream_t stream) {
+  g_msg[0] = 0;
+  if (key_mask == nullptr)
+    return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_attention_masked: null key_mask");
+  if (!aligned(key_mask, 4))
+    return fail(TFX_ERR_MISALIGNED, "tfx_attention_masked: key_mask must be 4-byte aligned");
+  return attention_checked("tfx_attention_masked", q, k, v, ld_qkv, out, ld_out, batch, heads,
+                           seq, head_dim, scale, causal, KeyMask{nullptr, key_mask},
+                           reinterpret_cast<cudaStream_t>(stream));
+}
+
 int tfx_attention(const tfx_half* q, const tfx_half* k, const tfx_half* v, int64_t ld_qkv,
                   tfx_half* out, int64_t ld_out, int batch, int heads, int seq, int head_dim,
                   float scale, int causal, const int32_t* valid_len, tfx_stream_t stream) {
   g_msg[0] = 0;
-  if (q == nullptr || k == nullptr || v == nullptr || out == nullptr)
-    return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_attention: null tensor");
-  if (batch <= 0 || heads <= 0 || seq <= 0 || head_dim <= 0)
-    return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_attention: sizes must be positive");
-  if (heads > 65535 || batch > 65535)
-    return fail(TFX_ERR_UNSUPPORTED, "tfx_attention: batch and heads must be <= 65535");
-  if (ld_qkv < static_cast<int64_t>(heads) * head_dim || ld_out < static_cast<int64_t>(heads) * head_dim)
-    return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_attention: leading dimension smaller than H*hd");
-  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(out, 16) ||
-      ld_qkv % 8 != 0 || ld_out % 8 != 0)
-    return fail(TFX_ERR_MISALIGNED,
-                "tfx_attention: pointers 16-byte aligned and leading dims multiples of 8 needed");
-  return launch_attention(reinterpret_cast<const __half*>(q), reinterpret_cast<const __half*>(k),
-                          reinterpret_cast<const __half*>(v), ld_qkv,
-                          reinterpret_cast<__half*>(out), ld_out, batch, heads, seq, head_dim,
-                          scale, causal, valid_len, reinterpret_cast<cudaStream_t>(stream));
+  return attention_checked("tfx_attention", q, k, v, ld_qkv, out, ld_out, batch, heads, seq,
+                           head_dim, scale, causal, KeyMask{valid_len, nullptr},
+                           reinterpret_cast<cudaStream_t>(stream));
 }
 
 int64_t tfx_attention_vt_ld(int seq) { return seq > 0 ? attention_vt_ld(seq) : -1; }
@@ -290,7 +314,7 @@ int tfx_attention_vt(const tfx_half* q, const tfx_half* k, const tfx_half* vt, i
                                 reinterpret_cast<const __half*>(k),
                                 reinterpret_cast<const __half*>(vt), ld_qkv,
                                 reinterpret_cast<__half*>(out), ld_out, batch, heads, seq,
-                                head_dim, scale, causal, valid_len,
+                                head_dim, scale, causal, KeyMask{valid_len, nullptr},
                                 reinterpret_cast<cudaStream_t>(stream));
 }
 

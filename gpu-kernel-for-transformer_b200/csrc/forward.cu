@@ -24,14 +24,18 @@
 namespace tfx {
 namespace {
 
+// Rows of padded tokens -> 0 (prefix lengths or a token bitmask).
 __global__ void zero_padded_rows_kernel(float* y, int seq, int d, const int32_t* valid_len,
-                                        int64_t rows) {
+                                        const uint32_t* key_bits, int key_words, int64_t rows) {
   grid_dep_wait();
   grid_dep_launch();
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
   if (row >= rows) return;
   const int b = static_cast<int>(row / seq), s = static_cast<int>(row % seq);
-  if (s < valid_len[b]) return;
+  const bool valid = valid_len != nullptr
+                         ? s < valid_len[b]
+                         : ((key_bits[static_cast<int64_t>(b) * key_words + s / 32] >> (s % 32)) & 1u);
+  if (valid) return;
   float4* yr = reinterpret_cast<float4*>(y + row * d);
   for (int c = threadIdx.x & 31; c < d / 4; c += 32) yr[c] = make_float4(0.f, 0.f, 0.f, 0.f);
 }
@@ -63,8 +67,8 @@ constexpr size_t kAlign = 256;
 
 // The model's own path setting decides (tfx_model.path); nothing here is
 // process-wide.
-bool use_fused(const tfx_model* m, int seq, const int32_t* valid_len) {
-  return m->path == TFX_PATH_AUTO && fused_forward_supported(m, seq, valid_len);
+bool use_fused(const tfx_model* m, int seq) {
+  return m->path == TFX_PATH_AUTO && fused_forward_supported(m, seq);
 }
 
 // [a, a + a_bytes) and [b, b + b_bytes) share at least one byte.
@@ -158,8 +162,7 @@ struct KvCache {
 // layer's new K/V rows are appended to its cache, and the new tokens attend
 // every cached key (positions before theirs: causal with an offset).
 int run_chain(const tfx_model* model, const float* x, float* y, int batch, int seq,
-              const int32_t* valid_len, const Workspace& ws, cudaStream_t stream,
-              const KvCache* kv) {
+              const KeyMask& km, const Workspace& ws, cudaStream_t stream, const KvCache* kv) {
   const int64_t m = static_cast<int64_t>(batch) * seq;
   const int d = model->d_model, f = model->ffn_dim, nh = model->num_heads, hd = d / nh;
   const float eps = model->eps;
@@ -198,10 +201,10 @@ int run_chain(const tfx_model* model, const float* x, float* y, int batch, int s
       st = launch_transpose_v(ws.qkv + 2 * d, 3 * d, ws.h, batch, seq, d, stream);
       if (st != TFX_OK) return st;
       st = launch_attention_tc_vt(ws.qkv, ws.qkv + d, ws.h, 3 * d, ws.ctx, d, batch, nh, seq, hd,
-                                  scale, model->causal, valid_len, stream);
+                                  scale, model->causal, km, stream);
     } else {
       st = launch_attention(ws.qkv, ws.qkv + d, ws.qkv + 2 * d, 3 * d, ws.ctx, d, batch, nh, seq,
-                            hd, scale, model->causal, valid_len, stream);
+                            hd, scale, model->causal, km, stream);
     }
     if (st != TFX_OK) return st;
     st = launch_linear(ws.ctx, d, reinterpret_cast<const __half*>(L.out_weight), L.out_bias,
@@ -227,15 +230,39 @@ int run_chain(const tfx_model* model, const float* x, float* y, int batch, int s
     }
     if (st != TFX_OK) return st;
   }
-  if (valid_len != nullptr) {
+  if (km.any()) {
     const int64_t blocks = (m + 7) / 8;
     launch_pdl(zero_padded_rows_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream,
-               y, seq, d, valid_len, m);
+               y, seq, d, km.len, km.bits, key_words(seq), m);
     st = check_launch("zero_padded_rows_kernel");
   }
   return st;
 }
 
+
+int forward_impl(const char* fn, const tfx_model* model, const float* x, float* y, int batch,
+                 int seq, const KeyMask& km, void* workspace, size_t workspace_bytes,
+                 cudaStream_t stream) {
+  int st = check_model(model);
+  if (st != TFX_OK) return st;
+  if (x == nullptr || y == nullptr) return fail(TFX_ERR_INVALID_ARGUMENT, "%s: null x or y", fn);
+  if (batch <= 0 || seq <= 0)
+    return fail(TFX_ERR_INVALID_ARGUMENT, "%s: batch and seq must be positive", fn);
+  const size_t act_bytes = sizeof(float) * static_cast<size_t>(batch) * seq * model->d_model;
+  if (ranges_overlap(x, act_bytes, y, act_bytes))
+    return fail(TFX_ERR_INVALID_ARGUMENT, "%s: y must not overlap x", fn);
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(y) % 16 ||
+      reinterpret_cast<uintptr_t>(workspace) % kAlign)
+    return fail(TFX_ERR_MISALIGNED, "%s: x/y 16-byte and workspace 256-byte alignment", fn);
+  if (use_fused(model, seq)) return launch_fused_forward(model, x, y, batch, seq, km, stream);
+  if (workspace == nullptr) return fail(TFX_ERR_INVALID_ARGUMENT, "%s: null workspace", fn);
+  const int d = model->d_model, f = model->ffn_dim, hd = d / model->num_heads;
+  const Workspace ws = plan_workspace(static_cast<char*>(workspace), batch, seq, d, f, hd);
+  if (workspace_bytes < ws.bytes)
+    return fail(TFX_ERR_WORKSPACE, "%s: workspace %zu < required %zu bytes", fn, workspace_bytes,
+                ws.bytes);
+  return run_chain(model, x, y, batch, seq, km, ws, stream, nullptr);
+}
 
 }  // namespace
 }  // namespace tfx
@@ -246,7 +273,7 @@ extern "C" {
 
 int64_t tfx_forward_workspace_bytes(const tfx_model* model, int batch, int seq) {
   if (check_model(model) != TFX_OK || batch <= 0 || seq <= 0) return -1;
-  if (use_fused(model, seq, nullptr)) return 0;
+  if (use_fused(model, seq)) return 0;
   return static_cast<int64_t>(plan_workspace(nullptr, batch, seq, model->d_model, model->ffn_dim,
                                             model->d_model / model->num_heads)
                                  .bytes);
@@ -255,30 +282,23 @@ int64_t tfx_forward_workspace_bytes(const tfx_model* model, int batch, int seq) 
 int tfx_forward(const tfx_model* model, const float* x, float* y, int batch, int seq,
                 const int32_t* valid_len, void* workspace, size_t workspace_bytes,
                 tfx_stream_t stream_) {
-  int st = check_model(model);
-  if (st != TFX_OK) return st;
-  if (x == nullptr || y == nullptr)
-    return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward: null x or y");
-  if (batch <= 0 || seq <= 0)
-    return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward: batch and seq must be positive");
-  const size_t act_bytes = sizeof(float) * static_cast<size_t>(batch) * seq * model->d_model;
-  if (ranges_overlap(x, act_bytes, y, act_bytes))
-    return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward: y must not overlap x");
-  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(y) % 16 ||
-      reinterpret_cast<uintptr_t>(workspace) % kAlign)
-    return fail(TFX_ERR_MISALIGNED, "tfx_forward: x/y 16-byte and workspace 256-byte alignment");
-  if (use_fused(model, seq, valid_len))
-    return launch_fused_forward(model, x, y, batch, seq, valid_len,
-                                reinterpret_cast<cudaStream_t>(stream_));
-  if (workspace == nullptr)
-    return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward: null workspace");
-  const int d = model->d_model, f = model->ffn_dim, hd = d / model->num_heads;
-  const Workspace ws = plan_workspace(static_cast<char*>(workspace), batch, seq, d, f, hd);
-  if (workspace_bytes < ws.bytes)
-    return fail(TFX_ERR_WORKSPACE, "tfx_forward: workspace %zu < required %zu bytes",
-                workspace_bytes, ws.bytes);
-  return run_chain(model, x, y, batch, seq, valid_len, ws, reinterpret_cast<cudaStream_t>(stream_),
-                   nullptr);
+  KeyMask km;
+  km.len = valid_len;
+  return forward_impl("tfx_forward", model, x, y, batch, seq, km, workspace, workspace_bytes,
+                      reinterpret_cast<cudaStream_t>(stream_));
+}
+
+int tfx_forward_masked(const tfx_model* model, const float* x, float* y, int batch, int seq,
+                       const uint32_t* key_mask, void* workspace, size_t workspace_bytes,
+                       tfx_stream_t stream_) {
+  if (key_mask == nullptr)
+    return fail(TFX_ERR_INVALID_ARGUMENT, "tfx_forward_masked: null key_mask");
+  if (reinterpret_cast<uintptr_t>(key_mask) % 4)
+    return fail(TFX_ERR_MISALIGNED, "tfx_forward_masked: key_mask must be 4-byte aligned");
+  KeyMask km;
+  km.bits = key_mask;
+  return forward_impl("tfx_forward_masked", model, x, y, batch, seq, km, workspace,
+                      workspace_bytes, reinterpret_cast<cudaStream_t>(stream_));
 }
 
 int64_t tfx_forward_kv_workspace_bytes(const tfx_model* model, int batch, int new_tokens) {
@@ -322,7 +342,7 @@ int tfx_forward_kv(const tfx_model* model, const float* x, float* y, int batch, 
                 workspace_bytes, ws.bytes);
   const KvCache kv{static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), capacity,
                    cache_len};
-  return run_chain(model, x, y, batch, new_tokens, nullptr, ws,
+  return run_chain(model, x, y, batch, new_tokens, KeyMask{}, ws,
                    reinterpret_cast<cudaStream_t>(stream_), &kv);
 }
 

@@ -1,6 +1,7 @@
 // Whole-forward fused kernel for the narrow configs: d_model = ffn_dim = 128,
 // seq_len dividing 128, head_dim in {16, 32, 64, 128}, with or without a
-// prefix padding mask (per-sequence valid lengths).
+// padding mask (per-sequence prefix lengths, or a token bitmask of any
+// pattern).
 //
 // A tile is 128 consecutive token rows = 128/seq_len whole sequences, so
 // attention never leaves the tile. One persistent CTA per SM takes tiles
@@ -79,6 +80,8 @@ struct FusedParams {
   const float* x;
   float* y;
   const int32_t* valid_len;  // nullable: [batch] prefix lengths (padding mask)
+  const uint32_t* key_bits;  // nullable: [batch][key_words] token bitmask (any padding)
+  int key_words;
   int64_t rows;
   int num_layers;
   int seq;
@@ -335,6 +338,27 @@ __device__ __forceinline__ void residual_read(uint32_t tl, int half, const float
 #pragma unroll
     for (int j = 0; j < 32; ++j) x[c][j] = __uint_as_float(rx[c][j]);
   if (next_bias != nullptr) store_x_biased(tl, half, next_bias, x);
+}
+
+// Validity bits of tile tokens [32*ch, 32*ch + 32) from the per-sequence key
+// bitmask (bit j = token 32*ch + j of the tile). seq divides 128: for
+// seq >= 32 the chunk is one aligned word of one sequence; for seq < 32 it
+// holds 32/seq whole sequences, one word each. Tokens past the batch: 0.
+__device__ __forceinline__ uint32_t tile_key_word(const FusedParams& p, int tile, int ch) {
+  const int64_t t0 = static_cast<int64_t>(tile) * kT + 32 * ch;
+  const int S = p.seq;
+  if (S >= 32) {
+    if (t0 >= p.rows) return 0u;
+    return p.key_bits[(t0 / S) * p.key_words + static_cast<int>(t0 % S) / 32];
+  }
+  const uint32_t low = (1u << S) - 1u;
+  uint32_t w = 0u;
+  for (int i = 0; i < 32 / S; ++i) {
+    const int64_t t = t0 + static_cast<int64_t>(i) * S;
+    if (t >= p.rows) break;
+    w |= (p.key_bits[(t / S) * p.key_words] & low) << (i * S);
+  }
+  return w;
 }
 
 template <int HD>
@@ -633,10 +657,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int len1 = (p.valid_len != nullptr && gt1 < p.rows) ? p.valid_len[gt1 / S] : S;
       const int key_hi0 = min(khn0, seq_lo0 + len - 1);  // padded keys masked
       const int key_hi1 = min(khn1, seq_lo1 + len1 - 1);
-      const bool row_valid = (r - seq_lo0) < len;  // not a padded token
+      bool row_valid = (r - seq_lo0) < len;  // not a padded token
+      // Key bitmask: the words of this warp's two key chunks (all ones
+      // without one) and this lane's own token bit.
+      uint32_t kw0 = 0xffffffffu, kw1 = 0xffffffffu;
+      if (p.key_bits != nullptr) {
+        kw0 = tile_key_word(p, tile, 2 * half);
+        kw1 = tile_key_word(p, tile, 2 * half + 1);
+        row_valid = (tile_key_word(p, tile, q) >> lane) & 1u;
+      }
       // A chunk needs no masking when every key in it is valid for every row
       // of this warp: whole-tile sequences, no padding, below the diagonal.
-      const bool plain_tile = (S == kT) && (p.valid_len == nullptr);
+      const bool plain_tile = (S == kT) && (p.valid_len == nullptr) && (p.key_bits == nullptr);
       float xv[2][32];  // this warp's 64 columns of the fp32 residual row
       {
         const float4* x4 = reinterpret_cast<const float4*>(p.x + grow * kT + 64 * half);
@@ -757,6 +789,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (plain_tile) {
 #pragma unroll
                 for (int j = 0; j < 32; ++j) sc[j] = j <= jhi ? sc[j] : -INFINITY;
+              } else if (p.key_bits != nullptr) {
+                const uint32_t cw = c ? kw1 : kw0;
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  sc[j] = (j >= jlo && j <= jhi && ((cw >> j) & 1u)) ? sc[j] : -INFINITY;
               } else {
 #pragma unroll
                 for (int j = 0; j < 32; ++j) sc[j] = (j >= jlo && j <= jhi) ? sc[j] : -INFINITY;
@@ -894,7 +931,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace
 
-bool fused_forward_supported(const tfx_model* m, int seq, const int32_t* /*valid_len*/) {
+bool fused_forward_supported(const tfx_model* m, int seq) {
   if (m->d_model != kT || m->ffn_dim != kT) return false;
   if (m->num_layers > kFusedMaxLayers || seq <= 0 || kT % seq != 0) return false;
   const int hd = m->d_model / m->num_heads;
@@ -902,7 +939,7 @@ bool fused_forward_supported(const tfx_model* m, int seq, const int32_t* /*valid
 }
 
 int launch_fused_forward(const tfx_model* m, const float* x, float* y, int batch, int seq,
-                         const int32_t* valid_len, cudaStream_t stream) {
+                         const KeyMask& km, cudaStream_t stream) {
   FusedParams p;
   memset(&p, 0, sizeof(p));
   for (int l = 0; l < m->num_layers; ++l) {
@@ -932,7 +969,9 @@ int launch_fused_forward(const tfx_model* m, const float* x, float* y, int batch
   p.lnf_b = m->final_norm_bias;
   p.x = x;
   p.y = y;
-  p.valid_len = valid_len;
+  p.valid_len = km.len;
+  p.key_bits = km.bits;
+  p.key_words = key_words(seq);
   p.rows = static_cast<int64_t>(batch) * seq;
   p.num_layers = m->num_layers;
   p.seq = seq;

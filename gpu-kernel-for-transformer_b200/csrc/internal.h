@@ -65,6 +65,17 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
 int make_tmap_3d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t batch, uint64_t cols,
                  uint64_t ld, uint64_t batch_stride, uint32_t box_cols, uint32_t box_rows);
 
+// Which keys of each sequence attention may use, and which output rows are
+// real tokens: all of them (both null), a prefix per sequence (len: [batch]
+// int32 valid lengths), or any pattern (bits: [batch][key_words(seq)] uint32,
+// bit k of word w set = token 32w+k is valid). At most one is set.
+struct KeyMask {
+  const int32_t* len = nullptr;
+  const uint32_t* bits = nullptr;
+  bool any() const { return len != nullptr || bits != nullptr; }
+};
+inline int key_words(int seq) { return (seq + 31) / 32; }
+
 // Kernel launchers (validated by the C-ABI layer before they are called).
 int launch_layer_norm(const float* x, const float* gamma, const float* beta, void* y, int y_dtype,
                       int64_t rows, int d, float eps, int apply_affine, cudaStream_t stream);
@@ -77,7 +88,7 @@ int launch_linear(const __half* a, int64_t lda, const __half* w, const float* bi
                   int k, int epilogue, cudaStream_t stream);
 int launch_attention(const __half* q, const __half* k, const __half* v, int64_t ld_qkv,
                      __half* out, int64_t ld_out, int batch, int heads, int seq, int head_dim,
-                     float scale, int causal, const int32_t* valid_len, cudaStream_t stream);
+                     float scale, int causal, const KeyMask& km, cudaStream_t stream);
 
 // Where an attention call's keys and values live relative to its queries.
 // Self-attention: interleaved with the queries ({ld_qkv, seq, seq, 0}). KV
@@ -110,7 +121,7 @@ int launch_attention_kv(const __half* q, int64_t ld_q, const __half* k, const __
 bool attention_tc_supported(int head_dim, float scale);
 int launch_attention_tc(const __half* q, const __half* k, const __half* v, int64_t ld_qkv,
                         __half* out, int64_t ld_out, int batch, int heads, int seq, int head_dim,
-                        float scale, int causal, const int32_t* valid_len, cudaStream_t stream);
+                        float scale, int causal, const KeyMask& km, cudaStream_t stream);
 // Same kernel reading V from a transposed copy vt[b][h*hd + d][s] (row pitch
 // attention_vt_ld(seq) elements), written by launch_transpose_v from the
 // packed projection; the P.V products then use a K-major operand.
@@ -122,12 +133,12 @@ int launch_attention_tc_kv(const __half* q, int64_t ld_q, const __half* k, const
                            int q_len, int head_dim, float scale, cudaStream_t stream);
 int launch_attention_tc_vt(const __half* q, const __half* k, const __half* vt, int64_t ld_qkv,
                            __half* out, int64_t ld_out, int batch, int heads, int seq,
-                           int head_dim, float scale, int causal, const int32_t* valid_len,
+                           int head_dim, float scale, int causal, const KeyMask& km,
                            cudaStream_t stream);
 
 // Whole-forward fused kernel (d_model = ffn_dim = 128, seq | 128).
-bool fused_forward_supported(const tfx_model* m, int seq, const int32_t* valid_len);
+bool fused_forward_supported(const tfx_model* m, int seq);
 int launch_fused_forward(const tfx_model* m, const float* x, float* y, int batch, int seq,
-                         const int32_t* valid_len, cudaStream_t stream);
+                         const KeyMask& km, cudaStream_t stream);
 
 }  // namespace tfx

@@ -207,6 +207,20 @@ def _plan_for(config: TransformerConfig) -> ShapeExecutionPlan:
     )
 
 
+def key_bitmask(mask: torch.Tensor) -> torch.Tensor:
+    """[B, S] bool -> int32 [B, ceil(S/32)]: bit k of word w of row b is
+    mask[b, 32*w + k] (the key_mask layout of tfx_forward_masked)."""
+    b, s = mask.shape
+    words = (s + 31) // 32
+    m = torch.zeros(b, words * 32, dtype=torch.int64, device=mask.device)
+    m[:, :s] = mask
+    weights = torch.ones(32, dtype=torch.int64, device=mask.device) << torch.arange(
+        32, dtype=torch.int64, device=mask.device)
+    w = (m.view(b, words, 32) * weights).sum(dim=-1)  # in [0, 2^32)
+    w = torch.where(w >= 2 ** 31, w - 2 ** 32, w)     # same bits as int32
+    return w.to(torch.int32).contiguous()
+
+
 def _version(t: torch.Tensor) -> Optional[int]:
     try:
         return t._version
@@ -444,7 +458,14 @@ class UserOptimizedTransformer(BaselineTransformer):
 
     # ------------------------------------------------------------- masks
     def _valid_lengths(self, x: torch.Tensor, mask: Optional[torch.Tensor]):
-        """All-True (or None) -> None; prefix-valid mask -> int32 lengths.
+        """The padding mask in the form the kernels take.
+
+        All-True (or None) -> None; a prefix-valid mask (the form the
+        reference's generator makes) -> int32 lengths [B]; any other mask ->
+        the token bitmask int32 [B, ceil(S/32)] (bit k of word w = token
+        32w+k is valid), which masks those keys in every layer and zeroes
+        their output rows, as the reference does for any [B, S] bool mask
+        (torch_transformer_benchmark.py:237-253, 496-510).
 
         Inspected once per mask object and version, like the reference's
         cached mask preparation (torch_transformer_benchmark.py:464-522),
@@ -464,12 +485,7 @@ class UserOptimizedTransformer(BaselineTransformer):
         else:
             lengths = m.sum(dim=1, dtype=torch.int32)
             prefix = torch.arange(m.shape[1], device=m.device)[None, :] < lengths[:, None]
-            if not bool(torch.equal(prefix, m)):
-                raise NotImplementedError(
-                    "only prefix-valid padding masks (the reference's generator form) are "
-                    "supported"
-                )
-            result = lengths.contiguous()
+            result = lengths.contiguous() if bool(torch.equal(prefix, m)) else key_bitmask(m)
         if ver is not None:
             self._mask_cache = (mask, ver, result)
         return result
@@ -503,12 +519,23 @@ class UserOptimizedTransformer(BaselineTransformer):
                  valid_len: Optional[torch.Tensor] = None,
                  workspace: Optional[torch.Tensor] = None) -> None:
         """Enqueue the forward of ``x`` into the preallocated ``y`` (no
-        allocation when ``workspace`` is given: safe inside graph capture)."""
+        allocation when ``workspace`` is given: safe inside graph capture).
+        ``valid_len`` is what ``_valid_lengths`` returns: None, int32
+        lengths [B], or the int32 token bitmask [B, ceil(S/32)]."""
         _, _, _, model = self._prepare(x.device)
         batch, seq, _ = x.shape
         if workspace is None:
             workspace = self._workspace_for(x.device, model, batch, seq)
         stream = torch.cuda.current_stream(x.device).cuda_stream
+        if valid_len is not None and valid_len.dim() == 2:  # token bitmask
+            _lib.check(
+                _lib.load().tfx_forward_masked(
+                    ctypes.byref(model), x.data_ptr(), y.data_ptr(), batch, seq,
+                    valid_len.data_ptr(), workspace.data_ptr(), workspace.numel(), stream,
+                ),
+                "tfx_forward_masked",
+            )
+            return
         _lib.check(
             _lib.load().tfx_forward(
                 ctypes.byref(model), x.data_ptr(), y.data_ptr(), batch, seq,

@@ -176,8 +176,12 @@ def attention(
     is_causal: bool = True,
     scale: Optional[float] = None,
     valid_lengths: Optional[torch.Tensor] = None,
+    key_mask: Optional[torch.Tensor] = None,
 ) -> torch.Tensor:
     """Flash attention on [B, S, H, hd] views (e.g. slices of the packed QKV).
+
+    Key padding: ``valid_lengths`` (int [B], keys >= length masked) or
+    ``key_mask`` (bool [B, S], False = masked key, any pattern), not both.
 
     q, k, v: fp16 tensors indexed (b, s, h, e) whose last two dims are
     contiguous and which share the same row stride (the packed projection's
@@ -199,6 +203,23 @@ def attention(
     if scale is None:
         scale = hd ** -0.5
     out = torch.empty((bsz, seq, heads * hd), device=q.device, dtype=torch.float16)
+    if key_mask is not None:
+        if valid_lengths is not None:
+            raise ValueError("pass valid_lengths or key_mask, not both")
+        if key_mask.shape != (bsz, seq) or key_mask.dtype != torch.bool:
+            raise ValueError("key_mask must be a [B, S] bool tensor")
+        from .model import key_bitmask
+
+        words = key_bitmask(key_mask.to(q.device))
+        _lib.check(
+            _lib.load().tfx_attention_masked(
+                q.data_ptr(), k.data_ptr(), v.data_ptr(), q.stride(1), out.data_ptr(),
+                heads * hd, bsz, heads, seq, hd, float(scale), int(is_causal), words.data_ptr(),
+                _stream(q.device),
+            ),
+            "tfx_attention_masked",
+        )
+        return out
     vl_ptr = None
     if valid_lengths is not None:
         valid_lengths = valid_lengths.to(device=q.device, dtype=torch.int32).contiguous()

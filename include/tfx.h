@@ -118,6 +118,20 @@ TFX_API int tfx_attention(const tfx_half* q, const tfx_half* k, const tfx_half* 
                   float scale, int causal, const int32_t* valid_len, tfx_stream_t stream);
 
 /*
+ * tfx_attention with key padding of any pattern instead of prefix lengths:
+ * key_mask [batch][(seq + 31) / 32] uint32, bit k of word w of sequence b set
+ * = key 32*w + k of that sequence may be attended (4-byte aligned). A query
+ * whose visible keys are all masked gets a zero output row.
+ * Replaces: SDPA with the dense attn_mask = key_mask & causal_mask that
+ * _prepare_attention_args builds for padded inputs
+ * (torch_transformer_benchmark.py:496-510, 767-808).
+ */
+TFX_API int tfx_attention_masked(const tfx_half* q, const tfx_half* k, const tfx_half* v,
+                                 int64_t ld_qkv, tfx_half* out, int64_t ld_out, int batch,
+                                 int heads, int seq, int head_dim, float scale, int causal,
+                                 const uint32_t* key_mask, tfx_stream_t stream);
+
+/*
  * The attention path tfx_forward takes for head_dim 64 and 128, in its two
  * steps. No counterpart in the reference: V transposed is this library's
  * internal layout (the tcgen05 P.V products then read V as a K-major operand
@@ -197,6 +211,20 @@ TFX_API int64_t tfx_forward_workspace_bytes(const tfx_model* model, int batch, i
 TFX_API int tfx_forward(const tfx_model* model, const float* x, float* y, int batch, int seq,
                 const int32_t* valid_len, void* workspace, size_t workspace_bytes,
                 tfx_stream_t stream);
+
+/*
+ * tfx_forward with a padding mask of any pattern: key_mask [batch]
+ * [(seq + 31) / 32] uint32, bit k of word w of sequence b set = token 32*w+k
+ * is valid (4-byte aligned). Padded tokens are masked as keys in every
+ * layer and their output rows are zero, as in the reference's baseline
+ * (torch_transformer_benchmark.py:237-253, 288-289, 314-316). Same kernels,
+ * workspace and errors as tfx_forward.
+ * Replaces: _prepare_attention_args for a non-prefix valid_token_mask
+ * (torch_transformer_benchmark.py:464-522) and the masked forward it feeds.
+ */
+TFX_API int tfx_forward_masked(const tfx_model* model, const float* x, float* y, int batch,
+                               int seq, const uint32_t* key_mask, void* workspace,
+                               size_t workspace_bytes, tfx_stream_t stream);
 
 /*
  * tfx_forward without a workspace argument, for callers that cannot allocate

@@ -107,8 +107,9 @@ def test_linear(pkg, dev, m, n, k, epi):
     assert bool((err <= bound).all()), f"max err {err.max():.3g} at {int(err.argmax())}"
 
 
-def _attn_ref(q, k, v, causal, valid_len=None):
-    """fp64 softmax(QK^T/sqrt(hd)) V on [B, S, H, hd] fp16 inputs."""
+def _attn_ref(q, k, v, causal, valid_len=None, key_mask=None):
+    """fp64 softmax(QK^T/sqrt(hd)) V on [B, S, H, hd] fp16 inputs; a query
+    with no visible key gets a zero row."""
     b, s, h, hd = q.shape
     qd, kd, vd = (t.double().permute(0, 2, 1, 3) for t in (q, k, v))
     sc = (qd @ kd.transpose(-1, -2)) / math.sqrt(hd)
@@ -117,6 +118,8 @@ def _attn_ref(q, k, v, causal, valid_len=None):
     if valid_len is not None:
         keymask = torch.arange(s)[None, :] >= valid_len[:, None]
         sc = sc.masked_fill(keymask[:, None, None, :], float("-inf"))
+    if key_mask is not None:
+        sc = sc.masked_fill(~key_mask[:, None, None, :], float("-inf"))
     p = torch.softmax(sc, dim=-1)
     p = torch.nan_to_num(p, nan=0.0)
     return (p @ vd).permute(0, 2, 1, 3).reshape(b, s, h * hd)
@@ -211,6 +214,32 @@ def test_attention_transposed_v_path(pkg, dev, b, s, h, hd, causal, lengths):
                    "tfx_attention_vt")
     torch.cuda.synchronize()
     err = (out.double().cpu() - ref).abs().max().item()
+    assert err < 2e-3, err
+
+
+MASKED_CASES = [
+    # (batch, seq, heads, hd, causal): every head_dim, both kernels
+    (3, 128, 16, 8, True), (2, 70, 8, 16, False), (3, 200, 4, 32, True),
+    (2, 300, 4, 64, False), (2, 257, 2, 128, True), (1, 130, 2, 256, True),
+]
+
+
+@pytest.mark.parametrize("b,s,h,hd,causal", MASKED_CASES)
+def test_attention_arbitrary_key_mask(pkg, dev, b, s, h, hd, causal):
+    """tfx_attention_masked: random holes in the keys (about 30 %), whole
+    masked 128-key tiles and masked first keys (causal queries with no
+    visible key get zero rows)."""
+    qkv = _randn(b, s, 3, h, hd, seed=7 * s + hd).half()
+    g = torch.Generator().manual_seed(s + hd)
+    mask = torch.rand(b, s, generator=g) > 0.3
+    if s > 140:
+        mask[0, :130] = False  # a whole masked 128-key tile
+    mask[-1, 0] = False
+    ref = _attn_ref(qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2], causal, key_mask=mask)
+    gq = qkv.to(dev)
+    out = pkg.ops.attention(gq[:, :, 0], gq[:, :, 1], gq[:, :, 2], is_causal=causal,
+                            key_mask=mask.to(dev)).cpu()
+    err = (out.double() - ref).abs().max().item()
     assert err < 2e-3, err
 
 

@@ -235,3 +235,43 @@ def test_official_shapes_match_oracle(pkg, dev, shape_id):
     res = ob.compare_outputs(ref, y[:n], RTOL, ATOL)
     assert res.failed_elements == 0, (shape_id, res.failed_elements, res.max_abs_error)
     assert bool(torch.isfinite(y).all())
+
+
+HOLE_CASES = [
+    # (batch, seq, d_model, heads, ffn, layers, causal): fused kernel and chain
+    (9, 128, 128, 4, 128, 2, True),    # fused, one sequence per tile
+    (9, 32, 128, 4, 128, 2, False),    # fused, 4 sequences per tile
+    (40, 8, 128, 8, 128, 2, True),     # fused, 16 sequences per tile (seq < 32)
+    (3, 200, 128, 4, 128, 2, True),    # chain, head_dim 32 attention
+    (2, 261, 256, 4, 256, 2, False),   # chain, head_dim 64 (tcgen05, V transposed)
+    (2, 150, 256, 2, 256, 2, True),    # chain, head_dim 128
+    (4, 100, 128, 16, 128, 2, True),   # chain, head_dim 8
+]
+
+
+@pytest.mark.parametrize("case", HOLE_CASES)
+def test_arbitrary_padding_masks_match_oracle(pkg, dev, case):
+    """Padding masks with holes anywhere (not a prefix): the reference masks
+    those keys in every layer and zeroes their output rows
+    (torch_transformer_benchmark.py:237-253, 288-289, 314-316). Padded tokens
+    carry random inputs, so any leak into a valid row would show."""
+    b, s, d, h, f, l, causal = case
+    kw = dict(batch_size=b, seq_len=s, d_model=d, num_heads=h, ffn_dim=f, num_layers=l,
+              causal=causal)
+    oracle_model, cand = _pair(pkg, kw, 31, dev)
+    x = torch.randn(b, s, d, generator=torch.Generator().manual_seed(s))
+    mask = torch.rand(b, s, generator=torch.Generator().manual_seed(s + 1)) > 0.35
+    mask[0, 0] = False  # a causal query with no visible key
+    mask[-1] = True     # and one unpadded sequence
+    outs = []
+    for fused in (True, False):
+        cand.enable_fused_forward(fused)
+        with torch.inference_mode():
+            outs.append(cand(x.to(dev), mask.to(dev)).cpu())
+    with torch.inference_mode():
+        ref = oracle_model(x, mask)
+    for y in outs:
+        assert bool(torch.isfinite(y).all())
+        assert bool((y[~mask] == 0).all())
+        res = ob.compare_outputs(ref, y, RTOL, ATOL)
+        assert res.failed_elements == 0, (case, res.failed_elements, res.max_abs_error)

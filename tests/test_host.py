@@ -87,10 +87,29 @@ def test_mask_handling(pkg):
     assert lengths.dtype == torch.int32 and lengths.tolist() == [8, 5, 1]
     holes = mask.clone()
     holes[0, 3] = False
-    with pytest.raises(NotImplementedError):
-        m._valid_lengths(x, holes)
+    bits = m._valid_lengths(x, holes)
+    assert bits.dtype == torch.int32 and bits.shape == (3, 1)
+    assert bits[:, 0].tolist() == [0b11110111, 0b11111, 0b1]
     with pytest.raises(ValueError):
         m._valid_lengths(x, torch.ones(3, 7, dtype=torch.bool))
+
+
+def test_key_bitmask_layout(pkg):
+    """Bit k of word w of row b is mask[b, 32w + k], including bit 31 (sign)
+    and a ragged last word."""
+    from importlib import import_module
+
+    model = import_module(pkg.__name__ + ".model")
+    g = torch.Generator().manual_seed(0)
+    mask = torch.rand(4, 70, generator=g) > 0.5
+    mask[0, 31] = True
+    words = model.key_bitmask(mask)
+    assert words.shape == (4, 3) and words.dtype == torch.int32
+    u = words.to(torch.int64) & 0xFFFFFFFF
+    for b in range(4):
+        for t in range(70):
+            assert bool((u[b, t // 32] >> (t % 32)) & 1) == bool(mask[b, t])
+        assert int(u[b, 2]) >> 6 == 0  # bits past S are zero
 
 
 def test_no_cpu_fallback(pkg):
