@@ -650,10 +650,16 @@ int launch_decode_hd(const __half* q, int64_t ld_q, const __half* k, const __hal
 int launch_attention(const __half* q, const __half* k, const __half* v, int64_t ld_qkv,
                      __half* out, int64_t ld_out, int batch, int heads, int seq, int head_dim,
                      float scale, int causal, const KeyMask& km, cudaStream_t stream) {
-  // Head dims 64, 128 and 256 run on the tcgen05 kernel (attention_tc.cu).
+  // Head dims 64, 128 and 256 run on the tcgen05 kernel (attention_tc.cu);
+  // 8, 16 and 32 on its multi-head variant (attention_tc_small.cu) when the
+  // heads fill 64-column blocks. The mma.sync kernel below takes the rest
+  // (d_model 32: official shape 7) and KV-cache chunks.
   if (attention_tc_supported(head_dim, scale))
     return launch_attention_tc(q, k, v, ld_qkv, out, ld_out, batch, heads, seq, head_dim, scale,
                                causal, km, stream);
+  if (attention_tc_small_supported(head_dim, heads, batch, seq, scale))
+    return launch_attention_tc_small(q, k, v, ld_qkv, out, ld_out, batch, heads, seq, head_dim,
+                                     scale, causal, km, stream);
   return launch_mma(q, ld_qkv, k, v, AttnKv{ld_qkv, seq, seq, 0}, out, ld_out, batch, heads, seq,
                     head_dim, scale, causal, km, stream);
 }

@@ -122,6 +122,13 @@ bool attention_tc_supported(int head_dim, float scale);
 int launch_attention_tc(const __half* q, const __half* k, const __half* v, int64_t ld_qkv,
                         __half* out, int64_t ld_out, int batch, int heads, int seq, int head_dim,
                         float scale, int causal, const KeyMask& km, cudaStream_t stream);
+// tcgen05/TMEM flash attention for head_dim 8, 16 and 32: one CTA per 128
+// query rows and 64-column block of heads (heads * head_dim a multiple of 64).
+bool attention_tc_small_supported(int head_dim, int heads, int batch, int seq, float scale);
+int launch_attention_tc_small(const __half* q, const __half* k, const __half* v, int64_t ld_qkv,
+                              __half* out, int64_t ld_out, int batch, int heads, int seq,
+                              int head_dim, float scale, int causal, const KeyMask& km,
+                              cudaStream_t stream);
 // Same kernel reading V from a transposed copy vt[b][h*hd + d][s] (row pitch
 // attention_vt_ld(seq) elements), written by launch_transpose_v from the
 // packed projection; the P.V products then use a K-major operand.

@@ -143,6 +143,16 @@ ATTN_CASES = [
     (2, 257, 4, 64, False),
     (1, 513, 2, 128, False),
     (3, 129, 2, 128, True),
+    # head_dim 8/16/32 with heads filling 64-column blocks run the tcgen05
+    # multi-head kernel: many KV tiles (stage ring wraps), ragged blocks,
+    # non-causal, several head blocks per sequence.
+    (2, 1024, 4, 32, True),
+    (1, 700, 8, 16, False),
+    (2, 400, 16, 8, True),
+    (1, 385, 16, 8, False),
+    (2, 129, 8, 32, True),
+    # d_model 32 (official shape 7) stays on the mma.sync kernel
+    (2, 128, 4, 8, True),
 ]
 
 
@@ -157,10 +167,10 @@ def test_attention(pkg, dev, b, s, h, hd, causal):
     assert err < 2e-3, err
 
 
-@pytest.mark.parametrize("s,hd", [(128, 32), (300, 64), (300, 128)])
+@pytest.mark.parametrize("s,hd", [(128, 32), (300, 64), (300, 128), (300, 8), (260, 16)])
 def test_attention_key_padding(pkg, dev, s, hd):
     """Keys at or past valid_len are masked; length 0 gives a zero output."""
-    b, h = 4, 4
+    b, h = 4, 64 // hd if hd < 32 else 4
     qkv = _randn(b, s, 3, h, hd, seed=11 + hd).half()
     lengths = torch.tensor([s, 97, 5, 0], dtype=torch.int32)
     ref = _attn_ref(qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2], True, lengths)
