@@ -702,6 +702,9 @@ def measure(pkg, R, name, args, headline):
     gather_ms = None
     if R.world > 1:
         with torch.inference_mode():
+            # An untimed small gather first: NCCL sets up its peer
+            # connections on the first send/recv-based collective.
+            pkg.sharding.gather_shards(torch.zeros(stop - start, 8, device=R.dev), Bg, dst=0)
             R.barrier()
             t0 = time.perf_counter()
             full = pkg.sharding.gather_shards(y, Bg, dst=0)
