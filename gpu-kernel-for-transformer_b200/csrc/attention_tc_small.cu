@@ -389,12 +389,19 @@ __global__ void __launch_bounds__(kSmThreads, 1)
       ok = __all_sync(0xffffffffu,
                       mbar_wait(&o_done[(total - 1) & 1], ((total - 1) >> 1) & 1, err,
                                 kDevTimeoutAccum));
-    if (ok && q < seq && total == 0) {
+    // tcgen05.ld is warp-collective (.sync.aligned): the TMEM reads below run
+    // on every lane of the warp (ok and total are warp-uniform); only the
+    // global stores are predicated on the row being inside the sequence.
+    const bool store = q < seq;
+    if (ok && total == 0) {
       // No visible key at all (valid length 0): zero rows, O never computed.
-      uint4* d4 = reinterpret_cast<uint4*>(out + (static_cast<int64_t>(b) * seq + q) * ld_out + col0);
+      if (store) {
+        uint4* d4 =
+            reinterpret_cast<uint4*>(out + (static_cast<int64_t>(b) * seq + q) * ld_out + col0);
 #pragma unroll
-      for (int t = 0; t < 8; ++t) d4[t] = make_uint4(0u, 0u, 0u, 0u);
-    } else if (ok && q < seq) {
+        for (int t = 0; t < 8; ++t) d4[t] = make_uint4(0u, 0u, 0u, 0u);
+      }
+    } else if (ok) {
       tc_fence_after();
       __half* dst = out + (static_cast<int64_t>(b) * seq + q) * ld_out + col0;
 #pragma unroll
@@ -421,10 +428,12 @@ __global__ void __launch_bounds__(kSmThreads, 1)
                   pack_half2(__uint_as_float(o[2 * t]) * inv, __uint_as_float(o[2 * t + 1]) * inv);
           }
         }
-        uint4* d4 = reinterpret_cast<uint4*>(dst + g * HD);
+        if (store) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst + g * HD);
 #pragma unroll
-        for (int t = 0; t < HD / 8; ++t)
-          d4[t] = make_uint4(w[4 * t], w[4 * t + 1], w[4 * t + 2], w[4 * t + 3]);
+          for (int t = 0; t < HD / 8; ++t)
+            d4[t] = make_uint4(w[4 * t], w[4 * t + 1], w[4 * t + 2], w[4 * t + 3]);
+        }
       }
     }
   }
