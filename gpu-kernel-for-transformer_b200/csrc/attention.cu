@@ -652,8 +652,10 @@ int launch_attention(const __half* q, const __half* k, const __half* v, int64_t 
                      float scale, int causal, const KeyMask& km, cudaStream_t stream) {
   // Head dims 64, 128 and 256 run on the tcgen05 kernel (attention_tc.cu);
   // 8, 16 and 32 on its multi-head variant (attention_tc_small.cu) when the
-  // heads fill 64-column blocks. The mma.sync kernel below takes the rest
-  // (d_model 32: official shape 7) and KV-cache chunks.
+  // heads fill 64-column blocks and the sequence spans more than one
+  // 128-key tile. The mma.sync kernel below takes the rest (one-tile
+  // sequences, where it measured faster; d_model 32: official shape 7) and
+  // KV-cache chunks.
   if (attention_tc_supported(head_dim, scale))
     return launch_attention_tc(q, k, v, ld_qkv, out, ld_out, batch, heads, seq, head_dim, scale,
                                causal, km, stream);

@@ -31,7 +31,9 @@
 // set. Rows past the sequence end read as zeros (3-D tensor maps) and are
 // never stored.
 //
-// Replaces, for the narrow heads of official shapes 7, 11 (c4) and 13, the
+// Used for sequences longer than one 128-key tile (official shape 13 and
+// longer); shorter ones run the mma.sync kernel in attention.cu, which is
+// faster there (see attention_tc_small_supported). Replaces the
 // reference's SDPA call (torch_transformer_benchmark.py:767-808; the
 // reference forces the CUTLASS memory-efficient backend for head_dim 8,
 // :145-147, 788-799).
@@ -485,8 +487,15 @@ int launch_small_c(const __half* q, const __half* k, const __half* v, int64_t ld
 
 }  // namespace
 
+// Sequences of one 128-key tile stay on the mma.sync kernel: there a CTA's
+// work is a few small products per head and its latency, not the tensor
+// core, sets the time (one B200, per launch: B=64, S=128, H=16, head_dim 8:
+// mma.sync 13.6 us, this kernel 22.1 us; head_dim 16: 9.0 / 9.9; head_dim
+// 32: 7.2 / 7.0). From two tiles on this kernel is ahead (head_dim 32:
+// S=1024, B=64: 138.0 / 91.3 us; S=4096, B=8: 273.6 / 136.1 us).
 bool attention_tc_small_supported(int head_dim, int heads, int batch, int seq, float scale) {
   if (head_dim != 8 && head_dim != 16 && head_dim != 32) return false;
+  if (seq <= kSmTile) return false;
   const int64_t cols = static_cast<int64_t>(heads) * head_dim;
   return cols % 64 == 0 && scale > 0.f &&
          static_cast<int64_t>(batch) * (cols / 64) <= 0x7fffffffLL &&
