@@ -505,31 +505,41 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 }
 
 // vt[b][c][s] = v[b * seq + s][c] for c < cols, s < seq; zero for seq <= s < ld_vt.
-// 64 tokens x 64 columns per CTA through shared memory; 16-byte loads/stores.
+// Each lane transposes one 8-key x 8-column block in registers: eight 16-byte
+// row loads, 32 byte permutes, eight 16-byte column stores. A warp covers 32
+// keys x 64 columns (per load instruction 4 rows x 128 contiguous bytes; per
+// store 8 output rows x 64 contiguous bytes); a CTA of 8 warps 128 keys x
+// 128 columns. No shared memory: every lane keeps 8 loads in flight.
 __global__ void __launch_bounds__(256)
     transpose_v_kernel(const __half* __restrict__ v, int64_t ld_qkv, __half* __restrict__ vt,
                        int64_t ld_vt, int seq, int cols) {
   grid_dep_wait();
   grid_dep_launch();
-  __shared__ __align__(16) __half tile[64][64 + 8];
-  const int s0 = blockIdx.x * 64, c0 = blockIdx.y * 64, b = blockIdx.z;
-  for (int i = threadIdx.x; i < 64 * 8; i += blockDim.x) {
-    const int r = i >> 3, c = (i & 7) * 8;
-    uint4 val = make_uint4(0, 0, 0, 0);
-    if (s0 + r < seq)
-      val = *reinterpret_cast<const uint4*>(v + (static_cast<int64_t>(b) * seq + s0 + r) * ld_qkv +
-                                            c0 + c);
-    *reinterpret_cast<uint4*>(&tile[r][c]) = val;
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < 64 * 8; i += blockDim.x) {
-    const int c = i >> 3, s = (i & 7) * 8;
-    if (s0 + s >= ld_vt) continue;
-    __align__(16) __half h8[8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.z;
+  const int s0 = blockIdx.x * 128 + (warp & 3) * 32 + (lane >> 3) * 8;  // first key
+  const int c0 = blockIdx.y * 128 + (warp >> 2) * 64 + (lane & 7) * 8;   // first column
+  if (c0 >= cols || s0 >= ld_vt) return;
+  uint4 r[8];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) h8[k] = tile[s + k][c];
-    *reinterpret_cast<uint4*>(vt + (static_cast<int64_t>(b) * cols + c0 + c) * ld_vt + s0 + s) =
-        *reinterpret_cast<const uint4*>(h8);
+  for (int k = 0; k < 8; ++k)
+    r[k] = (s0 + k < seq) ? __ldcs(reinterpret_cast<const uint4*>(
+                                v + (static_cast<int64_t>(b) * seq + s0 + k) * ld_qkv + c0))
+                          : make_uint4(0u, 0u, 0u, 0u);
+  // Word j of row k holds columns 2j, 2j+1; word m of output column c holds
+  // keys 2m, 2m+1: low halves pair up for the even column, high for the odd.
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(r);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint32_t lo[4], hi[4];
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      lo[m] = __byte_perm(w[8 * m + j], w[8 * m + 4 + j], 0x5410);
+      hi[m] = __byte_perm(w[8 * m + j], w[8 * m + 4 + j], 0x7632);
+    }
+    __half* dst = vt + (static_cast<int64_t>(b) * cols + c0 + 2 * j) * ld_vt + s0;
+    __stcs(reinterpret_cast<uint4*>(dst), make_uint4(lo[0], lo[1], lo[2], lo[3]));
+    __stcs(reinterpret_cast<uint4*>(dst + ld_vt), make_uint4(hi[0], hi[1], hi[2], hi[3]));
   }
 }
 
@@ -626,7 +636,7 @@ int64_t attention_vt_ld(int seq) { return (static_cast<int64_t>(seq) + 7) / 8 * 
 int launch_transpose_v(const __half* v, int64_t ld_qkv, __half* vt, int batch, int seq,
                        int cols, cudaStream_t stream) {
   const int64_t ld_vt = attention_vt_ld(seq);
-  const dim3 grid(static_cast<unsigned>((ld_vt + 63) / 64), static_cast<unsigned>(cols / 64),
+  const dim3 grid(static_cast<unsigned>((ld_vt + 127) / 128), static_cast<unsigned>((cols + 127) / 128),
                   static_cast<unsigned>(batch));
   launch_pdl(transpose_v_kernel, grid, dim3(256), 0, stream, v, ld_qkv, vt, ld_vt, seq, cols);
   return check_launch("transpose_v_kernel");
