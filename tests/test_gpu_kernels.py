@@ -33,7 +33,8 @@ def _randn(*shape, seed=0, scale=1.0):
     return torch.randn(*shape, generator=g) * scale
 
 
-@pytest.mark.parametrize("rows,d", [(1, 128), (777, 128), (513, 1024), (64, 96), (33, 4096)])
+@pytest.mark.parametrize("rows,d", [(1, 128), (777, 128), (513, 1024), (64, 96), (33, 4096),
+                                    (40003, 128), (19001, 256)])  # last two: rows per warp > 1
 @pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32])
 def test_layer_norm(pkg, dev, rows, d, out_dtype):
     x = _randn(rows, d, seed=rows + d) * 3 + 0.5
@@ -45,7 +46,7 @@ def test_layer_norm(pkg, dev, rows, d, out_dtype):
     assert torch.allclose(got, ref, rtol=tol, atol=1e-5 + tol), (got - ref).abs().max()
 
 
-@pytest.mark.parametrize("rows,d", [(300, 128), (100, 1024)])
+@pytest.mark.parametrize("rows,d", [(300, 128), (100, 1024), (40001, 128)])
 @pytest.mark.parametrize("store", [True, False])
 def test_residual_layer_norm(pkg, dev, rows, d, store):
     r = _randn(rows, d, seed=3)
