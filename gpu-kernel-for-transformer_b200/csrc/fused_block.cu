@@ -1,5 +1,5 @@
 // Whole-forward fused kernel for the narrow configs: d_model = ffn_dim = 128,
-// seq_len dividing 128, head_dim in {16, 32, 64, 128}, with or without a
+// seq_len dividing 128, head_dim in {8, 16, 32, 64, 128}, with or without a
 // padding mask (per-sequence prefix lengths, or a token bitmask of any
 // pattern).
 //
@@ -97,7 +97,7 @@ namespace {
 constexpr int kT = 128;                      // tokens per tile = d_model = ffn_dim
 constexpr int kOpBytes = kT * kT * 2;        // one 128x128 fp16 operand (32 KB)
 constexpr int kBlkBytes = kT * 64 * 2;       // one 128-row x 64-col SW128 block (16 KB)
-constexpr int kWSlots = 3;
+constexpr int kWSlots = 3;  // weight ring slots (2 at head_dim 8, see kOffK2)
 // Per-layer parameter block in shared memory (floats).
 constexpr int kPQkv = 0, kPOut = 384, kPIn = 512, kPFo = 640;
 constexpr int kPLn1g = 768, kPLn1b = 896, kPLn2g = 1024, kPLn2b = 1152;
@@ -123,6 +123,12 @@ constexpr uint32_t kColO = 256;   // attention output buffers (2 x head_dim colu
 constexpr uint32_t kColF = 128;   // FFN-in accumulator
 constexpr uint32_t kColA = 256;   // fp16 A operand of the FFN GEMMs (64 columns)
 constexpr uint32_t kColX = 384;   // fp32 residual stream of the tile
+// head_dim 8: tcgen05's K = 16 spans a head pair, so K is staged twice with
+// the other parity's heads zeroed (copy 0: even heads, copy 1: odd heads);
+// copy 1 takes the third weight-ring slot, which runs with two slots.
+constexpr int kOffK2 = kOffW + 2 * kOpBytes;
+template <int HD>
+constexpr int weight_slots() { return HD == 8 ? 2 : kWSlots; }
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 // Byte address of row r, columns [c, c+8) of a K-major 128x128 fp16 operand
@@ -163,6 +169,22 @@ __device__ __forceinline__ void store_row(uint32_t base, int r, int c0, const fl
     sts128(sw_addr(base, r, c0 + 8 * j), pack_half2(v[8 * j], v[8 * j + 1]),
            pack_half2(v[8 * j + 2], v[8 * j + 3]), pack_half2(v[8 * j + 4], v[8 * j + 5]),
            pack_half2(v[8 * j + 6], v[8 * j + 7]));
+  }
+}
+
+// head_dim 8: columns [c0, c0+32) of token row r's K (four heads of 8) into
+// the two K copies: each head's 8 columns into the copy of its parity, zeros
+// into the other.
+__device__ __forceinline__ void store_k_split(uint32_t k0, uint32_t k1, int r, int c0,
+                                              const float* v) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int col = c0 + 8 * j;
+    const uint32_t a = sw_addr(((col >> 3) & 1) ? k1 : k0, r, col);
+    const uint32_t z = sw_addr(((col >> 3) & 1) ? k0 : k1, r, col);
+    sts128(a, pack_half2(v[8 * j], v[8 * j + 1]), pack_half2(v[8 * j + 2], v[8 * j + 3]),
+           pack_half2(v[8 * j + 4], v[8 * j + 5]), pack_half2(v[8 * j + 6], v[8 * j + 7]));
+    sts128(z, 0u, 0u, 0u, 0u);
   }
 }
 
@@ -442,6 +464,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------- weight producer
     int slot = 0;
     uint32_t ph = 0;
+    constexpr int WS = weight_slots<HD>();
     int issued[kWSlots];
     for (int s = 0; s < kWSlots; ++s) issued[s] = -1;
     bool ok = true;
@@ -466,7 +489,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_2d(dst, m, &w_full[slot], 0, row0);
           tma_load_2d(dst + kBlkBytes, m, &w_full[slot], 64, row0);
           issued[slot] = static_cast<int>(ph);
-          if (++slot == kWSlots) {
+          if (++slot == WS) {
             slot = 0;
             ph ^= 1;
           }
@@ -474,12 +497,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if (!ok)  // unwinding after a timeout: let our own copies land first
-      for (int s = 0; s < kWSlots; ++s)
+      for (int s = 0; s < WS; ++s)
         if (issued[s] >= 0) mbar_wait_sleep(&w_full[s], issued[s], nullptr, 0);
   } else if (warp == 1 && lane == 0) {
     // ----------------------------------------------------------- MMA issuer
     constexpr uint32_t id128 = idesc_f16_f32(128, 128);
-    constexpr uint32_t idhd = idesc_f16_f32(128, HD);
+    constexpr int WS = weight_slots<HD>();
+    constexpr int NPV = HD < 16 ? 16 : HD;  // P.V N: a head pair at head_dim 8
+    constexpr uint32_t idhd = idesc_f16_f32(128, NPV);
     int slot = 0;
     uint32_t ph = 0, c2m_ph = 0;
     uint32_t mph_o[2] = {0, 0};  // this thread's view of the O-buffer barriers
@@ -491,6 +516,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       return r;
     };
     const uint64_t dA = sdesc_k_sw128(sA), dK = sdesc_k_sw128(sK), dV = sdesc_k_sw128(sV);
+    const uint64_t dK2 = sdesc_k_sw128(sbase + kOffK2);  // head_dim 8: odd heads' K copy
     const uint64_t dW0 = sdesc_k_sw128(sbase + kOffW);
     auto take_w = [&](uint64_t& w) {
       if (!mbar_wait_sleep(&w_full[slot], ph, p.err, kDevTimeoutFull)) return false;
@@ -500,7 +526,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     auto release_w = [&]() {
       mma_commit(&w_empty[slot]);
-      if (++slot == kWSlots) {
+      if (++slot == WS) {
         slot = 0;
         ph ^= 1;
       }
@@ -517,7 +543,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       return true;
     };
     auto issue_s = [&](int h) {  // S_h = Q_h . K_h^T -> S buffer h % 2
-      mma_chain<HD / 16>(tmem + ((h & 1) ? kColS1 : kColS0), dA, h * HD, dK, h * HD, id128);
+      if constexpr (HD == 8)  // one K=16 step over the head pair; the K copy zeroes the other head
+        mma_chain<1>(tmem + ((h & 1) ? kColS1 : kColS0), dA, 16 * (h >> 1), (h & 1) ? dK2 : dK,
+                     16 * (h >> 1), id128);
+      else
+        mma_chain<HD / 16>(tmem + ((h & 1) ? kColS1 : kColS0), dA, h * HD, dK, h * HD, id128);
       mma_commit(&m2c_s[h & 1]);
     };
     bool ok = true;
@@ -551,10 +581,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t sb = (h & 1) ? kColS1 : kColS0;
           // P_h: keys [0,64) in columns [0,32) of its S buffer, keys [64,128)
           // in columns [64,96) (each compute warp packs over its own S half).
-          const uint64_t dVh = dV + static_cast<uint64_t>((h * HD * 128) >> 4);
+          const int vrow = HD == 8 ? 16 * (h >> 1) : h * HD;  // first V^T row (feature)
+          const uint64_t dVh = dV + static_cast<uint64_t>((vrow * 128) >> 4);
 #pragma unroll
           for (int k = 0; k < kT / 16; ++k)
-            mma_f16_ts(tmem + kColO + (h & 1) * HD, tmem + sb + (k < 4 ? 8 * k : 64 + 8 * (k - 4)),
+            mma_f16_ts(tmem + kColO + (h & 1) * NPV, tmem + sb + (k < 4 ? 8 * k : 64 + 8 * (k - 4)),
                        desc_col(dVh, 16 * k), idhd, k > 0 ? 1u : 0u);
           mma_commit(&m2c_o[h & 1]);
           if (h + 2 < H) {
@@ -620,10 +651,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int ch_hi0 = chunk_hi(qq0), ch_hi1 = chunk_hi(qq1);
     const float sl2 = p.scale_log2;
     // ctx_h = O_h / rowsum -> sA columns [h*HD + half*HD/2, +HD/2) (over Q_h).
+    // head_dim 8: the warp of the pair whose half matches the head's parity
+    // writes all 8 columns (O_h is this head's half of a 16-column product).
     auto write_ctx = [&](int h) {
       const float l = psum[((h & 1) * 2 + 0) * kT + r] + psum[((h & 1) * 2 + 1) * kT + r];
       const float inv = l > 0.f ? 1.0f / l : 0.f;
       const uint64_t inv2 = f2_pack(inv, inv);
+      if constexpr (HD == 8) {
+        if (half == (h & 1)) {  // warp-uniform
+          uint32_t o[8];
+          tmem_ld8(tl + kColO + (h & 1) * 16 + (h & 1) * 8, o);
+          tmem_ld_wait();
+          float v8[8];
+#pragma unroll
+          for (int j = 0; j < 8; j += 2)
+            f2_unpack(f2_mul(f2_pack(__uint_as_float(o[j]), __uint_as_float(o[j + 1])), inv2),
+                      v8[j], v8[j + 1]);
+          store_row<1>(sA, (h & 1) ? tok1 : tok0, h * HD, v8);  // token order
+        }
+        return;
+      }
       const uint32_t t_o = tl + kColO + (h & 1) * HD + half * HDH;
       float v[HDH];
       if constexpr (HDH == 8) {
@@ -738,7 +785,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (half == 0)
               store_q32<HD>(sA, r, 32 * (i + u), v[u]);
             else
-              store_row<4>(sK, r, 32 * (i + u), v[u]);
+              if constexpr (HD == 8)
+                store_k_split(sK, sbase + kOffK2, r, 32 * (i + u), v[u]);
+              else
+                store_row<4>(sK, r, 32 * (i + u), v[u]);
           }
         }
         if (half == 1 && !(ok = wait(m2c_g, ph_g))) break;  // keeps this warp's m2c_g phase
@@ -935,7 +985,7 @@ bool fused_forward_supported(const tfx_model* m, int seq) {
   if (m->d_model != kT || m->ffn_dim != kT) return false;
   if (m->num_layers > kFusedMaxLayers || seq <= 0 || kT % seq != 0) return false;
   const int hd = m->d_model / m->num_heads;
-  return hd == 16 || hd == 32 || hd == 64 || hd == 128;
+  return hd == 8 || hd == 16 || hd == 32 || hd == 64 || hd == 128;
 }
 
 int launch_fused_forward(const tfx_model* m, const float* x, float* y, int batch, int seq,
@@ -992,6 +1042,7 @@ int launch_fused_forward(const tfx_model* m, const float* x, float* y, int batch
     break;                                                                                      \
   }
   switch (hd) {
+    TFX_FUSED_CASE(8)
     TFX_FUSED_CASE(16)
     TFX_FUSED_CASE(32)
     TFX_FUSED_CASE(64)

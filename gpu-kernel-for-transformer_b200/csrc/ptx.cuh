@@ -506,6 +506,19 @@ __device__ __forceinline__ uint64_t exp2_poly_f2(uint64_t x) {
   return f2_pack(__uint_as_float(r0), __uint_as_float(r1));
 }
 
+// Per-warpgroup register limits (all 128 threads of a warpgroup execute
+// them together). The block's pool is its launch allocation (threads x
+// registers per thread); .inc blocks until other warpgroups' .dec have freed
+// enough of it, so the split must add up to the launch allocation.
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // Named barrier over `count` threads (a multiple of 32) with id `id` (1..15).
 // Arrive on named barrier `id` without waiting (pairs with named_bar_sync
 // by the other threads of the `count`).

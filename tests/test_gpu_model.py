@@ -124,6 +124,9 @@ FUSED_CASES = [
     # (batch, seq, d_model, heads, ffn, layers, causal[, padding_ratio])
     (4, 128, 128, 4, 128, 4, True),     # c1
     (300, 128, 128, 4, 128, 4, True),   # c2 geometry, several tiles per CTA
+    (3, 128, 128, 16, 128, 2, True),    # head_dim 8 (c4 geometry): zero-padded K copies
+    (5, 32, 128, 16, 128, 2, False),    # head_dim 8, 4 sequences per tile, non-causal
+    (9, 128, 128, 16, 128, 2, True, 0.5),  # head_dim 8, prefix padding
     (3, 128, 128, 8, 128, 2, True),     # head_dim 16
     (3, 128, 128, 2, 128, 2, True),     # head_dim 64
     (2, 128, 128, 1, 128, 2, True),     # head_dim 128
@@ -242,6 +245,7 @@ HOLE_CASES = [
     (9, 128, 128, 4, 128, 2, True),    # fused, one sequence per tile
     (9, 32, 128, 4, 128, 2, False),    # fused, 4 sequences per tile
     (40, 8, 128, 8, 128, 2, True),     # fused, 16 sequences per tile (seq < 32)
+    (9, 64, 128, 16, 128, 2, True),    # fused, head_dim 8
     (3, 200, 128, 4, 128, 2, True),    # chain, head_dim 32 attention
     (2, 261, 256, 4, 256, 2, False),   # chain, head_dim 64 (tcgen05, V transposed)
     (2, 150, 256, 2, 256, 2, True),    # chain, head_dim 128
