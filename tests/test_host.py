@@ -148,6 +148,22 @@ def test_package_baseline_forward_equals_oracle_on_holes(pkg):
         assert torch.allclose(model(x, mask), oracle_model(x, mask), atol=1e-6, rtol=0)
 
 
+def test_cpu_scenario_of_the_reference_validation(pkg):
+    """validate_transformer.py:77-104's CPU run (B=2, S=16, D=128, H=4,
+    F=512, 2 layers, FP32): the package's eager BaselineTransformer against
+    the oracle on two seeded trials."""
+    cfg = dict(batch_size=2, seq_len=16, d_model=128, num_heads=4, ffn_dim=512, num_layers=2,
+               causal=False)
+    oracle_model = ob.make_baseline(ob.TransformerConfig(**cfg), 1234)
+    torch.manual_seed(1234)
+    model = pkg.BaselineTransformer(pkg.TransformerConfig(**cfg)).eval()
+    for t in range(2):
+        x, mask = ob.generate_random_case(ob.TransformerConfig(**cfg), 1234 + t)
+        with torch.inference_mode():
+            res = ob.compare_outputs(oracle_model(x, mask), model(x, mask), 0.02, 0.002)
+        assert res.failed_elements == 0 and res.max_abs_error < 1e-5
+
+
 def test_fused_toggle_is_per_module(pkg):
     cfg = pkg.TransformerConfig(2, 16, 64, 4, 96, 1, True)
     a = pkg.UserOptimizedTransformer(cfg)
