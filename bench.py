@@ -580,7 +580,6 @@ def measure(pkg, R, name, args, headline):
     x_host = x if not x.is_cuda else None
     x = x.to(R.dev)
     y = torch.empty_like(x)
-    out = {}
 
     # ---- value: whole-forward graph replays, input resident in HBM
     with torch.inference_mode():
