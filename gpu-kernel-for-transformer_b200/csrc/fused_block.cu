@@ -172,6 +172,21 @@ __device__ __forceinline__ void store_row(uint32_t base, int r, int c0, const fl
   }
 }
 
+// ctx row r, columns [c0, c0 + 8*N8) <- fp16(v) in this CTA's sA and, with
+// REMOTE, at the same place in the peer CTA's sA (distributed shared memory).
+template <int N8, bool REMOTE>
+__device__ __forceinline__ void store_ctx(uint32_t base, int r, int c0, const float* v,
+                                          uint32_t peer) {
+#pragma unroll
+  for (int j = 0; j < N8; ++j) {
+    const uint32_t addr = sw_addr(base, r, c0 + 8 * j);
+    const uint32_t a = pack_half2(v[8 * j], v[8 * j + 1]), b = pack_half2(v[8 * j + 2], v[8 * j + 3]);
+    const uint32_t c = pack_half2(v[8 * j + 4], v[8 * j + 5]), d = pack_half2(v[8 * j + 6], v[8 * j + 7]);
+    sts128(addr, a, b, c, d);
+    if constexpr (REMOTE) st_cluster_v4(mapa_shared(addr, peer), a, b, c, d);
+  }
+}
+
 // head_dim 8: columns [c0, c0+32) of token row r's K (four heads of 8) into
 // the two K copies: each head's 8 columns into the copy of its parity, zeros
 // into the other.
@@ -383,10 +398,30 @@ __device__ __forceinline__ uint32_t tile_key_word(const FusedParams& p, int tile
   return w;
 }
 
-template <int HD>
+// Tiles a CTA (SPLIT: a CTA pair) takes in turn: first_tile, then every
+// tile_stride-th (read where used: nothing stays live across the kernel).
+template <bool SPLIT>
+__device__ __forceinline__ int first_tile() {
+  return SPLIT ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+}
+template <bool SPLIT>
+__device__ __forceinline__ int tile_stride() {
+  return SPLIT ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+}
+
+// SPLIT: a cluster of two CTAs (on two SMs) carries each tile. Both compute
+// every phase of the tile, except that CTA r attends only heads
+// [r*H/2, (r+1)*H/2) -- the 64-column block r of Q, K and ctx -- and writes
+// that ctx block into its own and its peer's sA (distributed shared memory)
+// before the out-projection. Used when the batch has at most half as many
+// tiles as the GPU has SMs (c1, c4), where a tile's latency, not the SMs'
+// throughput, sets the time.
+template <int HD, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
     fused_forward_kernel(const __grid_constant__ FusedParams p) {
   constexpr int H = kT / HD;
+  constexpr int HL = SPLIT ? H / 2 : H;  // heads this CTA attends
+  static_assert(!SPLIT || H >= 2, "the split needs two heads");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -407,7 +442,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* c2m_p = m2c_o + 2;
   uint64_t* m2c_v = c2m_p + 2;  // MMA -> compute: V^T accumulator ready
   uint64_t* m2c_k = m2c_v + 1;  // MMA -> compute: K accumulator ready
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(m2c_k + 1);
+  // SPLIT only, arrived on by the PEER's compute warps (one per warp):
+  uint64_t* peer_ctx = m2c_k + 1;     // the peer's ctx block is in this CTA's sA
+  uint64_t* peer_free = peer_ctx + 1; // the peer's QKV products no longer read its sA
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(peer_free + 1);
+  const uint32_t rank = SPLIT ? cluster_ctarank() : 0u;
+  const uint32_t peer = rank ^ 1u;
+  const int h0 = static_cast<int>(rank) * HL, h1 = h0 + HL;
+
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -424,6 +466,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(m2c_v, 1);
     mbar_init(m2c_k, 1);
+    mbar_init(peer_ctx, kComputeWarps);
+    mbar_init(peer_free, kComputeWarps);
     fence_mbar_init();
   }
   grid_dep_wait();
@@ -457,6 +501,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // The peer arrives on this CTA's barriers: both CTAs' barriers are
+  // initialised before either goes on.
+  if constexpr (SPLIT) cluster_sync_all();
   const uint32_t tmem = *tmem_slot;
   const float* parf = par + kFusedMaxLayers * kParFloats;  // final LN gamma | beta
 
@@ -468,7 +515,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int issued[kWSlots];
     for (int s = 0; s < kWSlots; ++s) issued[s] = -1;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+    for (int tile = first_tile<SPLIT>(); tile < p.num_tiles && ok; tile += tile_stride<SPLIT>()) {
       // The producer runs ahead of the compute warps (here: about one layer
       // of the previous tile), so the tile's fp32 input is an L2 hit by the
       // time they load it.
@@ -509,6 +556,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t ph = 0, c2m_ph = 0;
     uint32_t mph_o[2] = {0, 0};  // this thread's view of the O-buffer barriers
     uint32_t mph_p[2] = {0, 0};  // ... and of the P-ready barriers
+    uint32_t ph_peer = 0;        // SPLIT: phase of peer_ctx
     auto wait_c2m = [&]() {
       const bool r = mbar_wait_sleep(c2m, c2m_ph, p.err, kDevTimeoutOther);
       c2m_ph ^= 1;
@@ -551,7 +599,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mma_commit(&m2c_s[h & 1]);
     };
     bool ok = true;
-    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+    for (int tile = first_tile<SPLIT>(); tile < p.num_tiles && ok; tile += tile_stride<SPLIT>()) {
       for (int l = 0; l < L && ok; ++l) {
         uint64_t w;
         if (!(ok = wait_c2m())) break;  // LN1 output in sA
@@ -571,9 +619,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         release_w();
         mma_commit(m2c_g);
         if (!(ok = wait_c2m())) break;  // Q, K, V^T in smem
-        issue_s(0);
-        if (H > 1) issue_s(1);
-        for (int h = 0; h < H && ok; ++h) {
+        issue_s(h0);
+        if (HL > 1) issue_s(h0 + 1);
+        for (int h = h0; h < h1 && ok; ++h) {
           // P_h written over S buffer h % 2 by all compute warps.
           if (!(ok = mbar_wait_sleep(&c2m_p[h & 1], mph_p[h & 1], p.err, kDevTimeoutOther))) break;
           mph_p[h & 1] ^= 1;
@@ -588,7 +636,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_f16_ts(tmem + kColO + (h & 1) * NPV, tmem + sb + (k < 4 ? 8 * k : 64 + 8 * (k - 4)),
                        desc_col(dVh, 16 * k), idhd, k > 0 ? 1u : 0u);
           mma_commit(&m2c_o[h & 1]);
-          if (h + 2 < H) {
+          if (h + 2 < h1) {
             // S_{h+2} reuses the columns P_h is read from: wait until P_h.V_h
             // has completed before overwriting them.
             if (!(ok = mbar_wait_sleep(&m2c_o[h & 1], mph_o[h & 1], p.err, kDevTimeoutOther))) break;
@@ -598,6 +646,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           mph_o[h & 1] ^= 1;
         }
         if (!ok || !(ok = wait_c2m())) break;  // ctx complete in sA
+        if constexpr (SPLIT) {  // and the peer's ctx block too
+          if (!(ok = mbar_wait_cluster(peer_ctx, ph_peer, p.err, kDevTimeoutOther))) break;
+          ph_peer ^= 1;
+          tc_fence_after();
+        }
         if (!(ok = take_w(w))) break;
         mma_chain<kT / 16>(tmem + kColX, dA, 0, w, 0, id128, 1u);  // x += out-proj
         release_w();
@@ -619,6 +672,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16);
     Pair pr{xch, half, r, 1 + q, 0};
     uint32_t ph_g = 0, ph_v = 0, ph_k = 0, ph_s[2] = {0, 0}, ph_o[2] = {0, 0};
+    uint32_t ph_pf = 0;  // SPLIT: phase of peer_free
     // Warp-uniform outcome: a timeout seen by one lane ends the whole warp.
     auto wait = [&](uint64_t* bar, uint32_t& phase) {
       const bool ok = __all_sync(0xffffffffu, mbar_wait_sleep(bar, phase, p.err, kDevTimeoutAccum));
@@ -667,7 +721,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < 8; j += 2)
             f2_unpack(f2_mul(f2_pack(__uint_as_float(o[j]), __uint_as_float(o[j + 1])), inv2),
                       v8[j], v8[j + 1]);
-          store_row<1>(sA, (h & 1) ? tok1 : tok0, h * HD, v8);  // token order
+          store_ctx<1, SPLIT>(sA, (h & 1) ? tok1 : tok0, h * HD, v8, peer);  // token order
         }
         return;
       }
@@ -693,10 +747,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                       v[16 * c + j], v[16 * c + j + 1]);
         }
       }
-      store_row<HDH / 8>(sA, (h & 1) ? tok1 : tok0, h * HD + half * HDH, v);  // token order
+      store_ctx<HDH / 8, SPLIT>(sA, (h & 1) ? tok1 : tok0, h * HD + half * HDH, v,
+                                peer);  // token order
     };
     bool ok = true;
-    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+    for (int tile = first_tile<SPLIT>(); tile < p.num_tiles && ok; tile += tile_stride<SPLIT>()) {
       const int64_t grow = static_cast<int64_t>(tile) * kT + r;
       const bool row_ok = grow < p.rows;
       const int64_t gt1 = static_cast<int64_t>(tile) * kT + tok1;
@@ -769,6 +824,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (half == 0 && !(ok = wait(m2c_g, ph_g))) break;
 #pragma unroll 1
         for (int i = 0; i < 4; i += 2) {  // Q chunks 0..3 (half 0) or K chunks 4..7 (half 1)
+          // SPLIT: only the 64-column block of this CTA's heads.
+          if (SPLIT && i != 2 * static_cast<int>(rank)) continue;
           uint32_t ra[32], rb[32];
           tmem_ld32(tl + 32 * (4 * half + i), ra);
           tmem_ld32(tl + 32 * (4 * half + i) + 32, rb);
@@ -793,9 +850,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (half == 1 && !(ok = wait(m2c_g, ph_g))) break;  // keeps this warp's m2c_g phase
         signal();
+        if constexpr (SPLIT) {
+          // This CTA's QKV products are complete (m2c_g): the block of sA the
+          // peer's heads own may now take the peer's ctx.
+          __syncwarp();
+          if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(peer_free), peer));
+        }
+        bool peer_free_seen = !SPLIT;
+        auto await_peer_free = [&]() {  // before the first ctx store into the peer
+          if (peer_free_seen) return true;
+          peer_free_seen = true;
+          const bool r2 =
+              __all_sync(0xffffffffu, mbar_wait_cluster(peer_free, ph_pf, p.err, kDevTimeoutOther));
+          ph_pf ^= 1;
+          return r2;
+        };
         // Attention, double-buffered over heads.
 #pragma unroll 1
-        for (int h = 0; h < H; ++h) {
+        for (int h = h0; h < h1; ++h) {
           const int b = h & 1;
           const uint32_t sb = tl + (b ? kColS1 : kColS0);
           if (!(ok = wait(&m2c_s[b], ph_s[b]))) break;
@@ -901,15 +973,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&c2m_p[b]);
-          if (h > 0) {  // overlap: finish the previous head while P.V runs
+          if (h > h0) {  // overlap: finish the previous head while P.V runs
             if (!(ok = wait(&m2c_o[b ^ 1], ph_o[b ^ 1]))) break;
+            if (!(ok = await_peer_free())) break;
             write_ctx(h - 1);
           }
         }
-        if (!ok || !(ok = wait(&m2c_o[(H - 1) & 1], ph_o[(H - 1) & 1]))) break;
+        if (!ok || !(ok = wait(&m2c_o[(h1 - 1) & 1], ph_o[(h1 - 1) & 1]))) break;
+        if (!(ok = await_peer_free())) break;
         named_bar_sync(pr.bar_id, 64);  // partner's row sum of the last head is visible
-        write_ctx(H - 1);
+        write_ctx(h1 - 1);
         signal();  // ctx complete
+        if constexpr (SPLIT) {
+          // This CTA's ctx block is in the peer's sA as well.
+          fence_proxy_async_cluster();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(peer_ctx), peer));
+        }
         if (!(ok = wait(m2c_g, ph_g))) break;  // out-proj accumulator
         {
           float mean, rstd, v[2][32];
@@ -956,7 +1036,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             store_row<4>(sA, r, 64 * half + 32, v[1]);
           } else {
             ln_apply(xv, mean, rstd, parf, parf + 128, half, v);
-            if (row_ok) {  // final output: padded tokens are zero rows
+            // Final output: padded tokens are zero rows. SPLIT: both CTAs hold
+            // the whole row; each stores the columns of its own half.
+            if (row_ok && (!SPLIT || half == static_cast<int>(rank))) {
               const float keep = row_valid ? 1.0f : 0.0f;
               float4* y4 = reinterpret_cast<float4*>(p.y + grow * kT + 64 * half);
 #pragma unroll
@@ -977,6 +1059,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, 512);
+  // No CTA leaves while its peer may still store into its shared memory or
+  // arrive on its barriers (also after a timeout).
+  if constexpr (SPLIT) cluster_sync_all();
 }
 
 }  // namespace
@@ -986,6 +1071,31 @@ bool fused_forward_supported(const tfx_model* m, int seq) {
   if (m->num_layers > kFusedMaxLayers || seq <= 0 || kT % seq != 0) return false;
   const int hd = m->d_model / m->num_heads;
   return hd == 8 || hd == 16 || hd == 32 || hd == 64 || hd == 128;
+}
+
+// Cluster launch (2 CTAs per cluster) with programmatic stream serialization.
+int launch_split(void (*kern)(FusedParams), int grid, const FusedParams& p, cudaStream_t stream,
+                 int* done) {
+  int st = ensure_smem(reinterpret_cast<const void*>(kern), kSmemBytes, done);
+  if (st != TFX_OK) return st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 2;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
+  if (e != cudaSuccess)
+    return fail(TFX_ERR_CUDA, "fused forward (CTA pairs): %s", cudaGetErrorString(e));
+  return TFX_OK;
 }
 
 int launch_fused_forward(const tfx_model* m, const float* x, float* y, int batch, int seq,
@@ -1031,14 +1141,25 @@ int launch_fused_forward(const tfx_model* m, const float* x, float* y, int batch
   const int hd = m->d_model / m->num_heads;
   p.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(hd));
   p.err = device_error_word();
-  const int grid = p.num_tiles < num_sms() ? p.num_tiles : num_sms();
+  const int sms = num_sms();
+  // Few tiles (at most one per two SMs): two CTAs per tile, heads split.
+  const bool split = hd < kT && 2 * p.num_tiles <= sms;
+  const int grid = split ? 2 * p.num_tiles : (p.num_tiles < sms ? p.num_tiles : sms);
   int st = TFX_OK;
 #define TFX_FUSED_CASE(HDV)                                                                     \
   case HDV: {                                                                                   \
-    static int done[kMaxDevices] = {0};                                                         \
-    st = ensure_smem(reinterpret_cast<const void*>(fused_forward_kernel<HDV>), kSmemBytes, done); \
+    if (split && HDV < kT) {                                                                    \
+      static int done_s[kMaxDevices] = {0};                                                     \
+      st = launch_split(fused_forward_kernel<HDV, (HDV < kT)>, grid, p, stream, done_s);        \
+    } else {                                                                                    \
+      static int done[kMaxDevices] = {0};                                                       \
+      st = ensure_smem(reinterpret_cast<const void*>(fused_forward_kernel<HDV, false>),         \
+                       kSmemBytes, done);                                                       \
+      if (st != TFX_OK) return st;                                                              \
+      launch_pdl(fused_forward_kernel<HDV, false>, dim3(grid), dim3(kThreads), kSmemBytes,      \
+                 stream, p);                                                                    \
+    }                                                                                           \
     if (st != TFX_OK) return st;                                                                \
-    launch_pdl(fused_forward_kernel<HDV>, dim3(grid), dim3(kThreads), kSmemBytes, stream, p);  \
     break;                                                                                      \
   }
   switch (hd) {

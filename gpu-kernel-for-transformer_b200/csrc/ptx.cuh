@@ -506,6 +506,70 @@ __device__ __forceinline__ uint64_t exp2_poly_f2(uint64_t x) {
   return f2_pack(__uint_as_float(r0), __uint_as_float(r1));
 }
 
+// ------------------------------------------------- thread-block clusters
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Shared::cluster address of the same shared-memory location in CTA `rank`
+// of this cluster (distributed shared memory).
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t cta_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(cta_addr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void st_cluster_v4(uint32_t cluster_addr, uint32_t a, uint32_t b,
+                                              uint32_t c, uint32_t d) {
+  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr), "r"(a),
+               "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+
+// Orders this thread's generic-proxy writes to shared::cluster memory (its
+// own or a peer's) before later async-proxy (tensor core, TMA) accesses.
+__device__ __forceinline__ void fence_proxy_async_cluster() {
+  asm volatile("fence.proxy.async.shared::cluster;" ::: "memory");
+}
+
+// Arrive on an mbarrier in another CTA of the cluster (release at cluster
+// scope: this thread's earlier writes are visible to whoever acquires it).
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_bar_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
+                   cluster_bar_addr)
+               : "memory");
+}
+
+// Bounded wait (acquire at cluster scope) on a local mbarrier that a peer
+// CTA arrives on; suspends between polls like mbar_wait_sleep.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* err,
+                                                  int code) {
+  const long long t0 = clock64();
+  while (true) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
+        : "memory");
+    if (ok) return true;
+    if (clock64() - t0 > kWaitLimitCycles) {
+      record_error(err, code);
+      return false;
+    }
+  }
+}
+
+// Cluster-wide barrier of every thread of every CTA in the cluster.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+
 // Per-warpgroup register limits (all 128 threads of a warpgroup execute
 // them together). The block's pool is its launch allocation (threads x
 // registers per thread); .inc blocks until other warpgroups' .dec have freed
