@@ -172,7 +172,7 @@ typedef struct tfx_layer {
 typedef enum tfx_path {
   TFX_PATH_AUTO = 0,  /* fused whole-forward kernel wherever it applies (d_model =
                          ffn_dim = 128, seq_len dividing 128, head_dim in
-                         {16, 32, 64, 128}, <= 5 layers), else the per-op chain */
+                         {8, 16, 32, 64, 128}, <= 5 layers), else the per-op chain */
   TFX_PATH_CHAIN = 1  /* always the per-op kernel chain */
 } tfx_path;
 
