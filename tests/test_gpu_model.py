@@ -279,3 +279,22 @@ def test_arbitrary_padding_masks_match_oracle(pkg, dev, case):
         assert bool((y[~mask] == 0).all())
         res = ob.compare_outputs(ref, y, RTOL, ATOL)
         assert res.failed_elements == 0, (case, res.failed_elements, res.max_abs_error)
+
+
+@pytest.mark.parametrize("heads,seq", [(4, 128), (16, 128), (8, 32), (2, 128)])
+def test_cta_pair_mode_equals_single_cta_mode(pkg, dev, heads, seq):
+    """A batch of few tiles runs each tile on a CTA pair (heads split, ctx
+    exchanged through distributed shared memory); a large batch runs one CTA
+    per tile. The per-tile arithmetic is the same, so the same sequences give
+    bit-identical outputs in both modes."""
+    kw = dict(batch_size=256, seq_len=seq, d_model=128, num_heads=heads, ffn_dim=128,
+              num_layers=2, causal=True)
+    _, cand = _pair(pkg, kw, 17, dev)
+    per_tile = 128 // seq
+    small_b = 8 * per_tile                    # 8 tiles: CTA pairs
+    big_b = 200 * per_tile                    # 200 tiles: more than half the SMs, one CTA each
+    x = torch.randn(big_b, seq, 128, generator=torch.Generator().manual_seed(heads + seq))
+    with torch.inference_mode():
+        y_big = cand(x.to(dev))
+        y_small = cand(x[:small_b].contiguous().to(dev))
+    assert torch.equal(y_small, y_big[:small_b])
