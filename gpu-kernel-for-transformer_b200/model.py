@@ -179,6 +179,7 @@ class ShapeExecutionPlan:
 
     official_shape_id: Optional[int]
     head_dim: int
+    path: str
     gemm_tiles: str
     attention: str
 
@@ -189,22 +190,37 @@ class ShapeExecutionPlan:
             else "general"
         )
         return (
-            f"{shape}: gemm=tcgen05 {self.gemm_tiles}, attention={self.attention} "
-            f"(head_dim {self.head_dim}), norm=fused fp32 LayerNorm"
+            f"{shape}: {self.path}; gemm=tcgen05 {self.gemm_tiles}, "
+            f"attention={self.attention} (head_dim {self.head_dim}), norm=fp32 LayerNorm"
         )
 
 
 def _plan_for(config: TransformerConfig) -> ShapeExecutionPlan:
+    """The dispatch the native runtime makes for this config (forward.cu,
+    fused_block.cu, attention.cu), as text."""
     ids = {c: i for i, c in OFFICIAL_BENCHMARK_SHAPES.items()}
-    hd = config.d_model // config.num_heads
-    widest = max(t for t in (256, 128, 64, 32) if config.d_model % t == 0) if \
-        config.d_model % 32 == 0 else 0
+    d, hd, s = config.d_model, config.d_model // config.num_heads, config.seq_len
+    fused = (d == 128 and config.ffn_dim == 128 and 128 % s == 0 and config.num_layers <= 5
+             and hd in (8, 16, 32, 64, 128))
+    if fused:
+        tiles = -(-config.batch_size * s // 128)
+        pairs = "one CTA per tile" if hd == 128 else (
+            f"a CTA pair per tile (heads split) on GPUs with at least {2 * tiles} SMs "
+            "(B200: 148), else one CTA per tile")
+        return ShapeExecutionPlan(
+            official_shape_id=ids.get(config), head_dim=hd,
+            path=f"fused whole-forward kernel, {tiles} tiles of 128 tokens, {pairs}",
+            gemm_tiles="128x128 in TMEM", attention="in-kernel tcgen05, S/P/O in TMEM")
+    if hd in (64, 128, 256):
+        attention = "tcgen05 flash (V transposed)" if hd != 256 else "tcgen05 flash"
+    elif (config.num_heads * hd) % 64 == 0 and s > 128:
+        attention = "tcgen05 flash, 64-column head blocks per CTA"
+    else:
+        attention = "mma.sync flash"
+    widest = max(t for t in (256, 192, 128, 64, 32) if d % t == 0) if d % 32 == 0 else 0
     return ShapeExecutionPlan(
-        official_shape_id=ids.get(config),
-        head_dim=hd,
-        gemm_tiles=f"128x{min(widest, 256)} persistent",
-        attention="flash (online softmax, streamed K/V)",
-    )
+        official_shape_id=ids.get(config), head_dim=hd, path="per-op kernel chain",
+        gemm_tiles=f"128x{min(widest, 256)} persistent", attention=attention)
 
 
 def key_bitmask(mask: torch.Tensor) -> torch.Tensor:
