@@ -9,7 +9,9 @@
 // with every intermediate on chip: HBM sees the fp32 input once and the fp32
 // output once (1 KB per token), instead of ~27 KB per token for the chain of
 // separate kernels. Weights (192 KB fp16 per layer) stream from L2 through a
-// TMA ring; biases and LayerNorm parameters sit in shared memory.
+// TMA ring; biases and LayerNorm parameters sit in shared memory. A tile's
+// fp32 input arrives by TMA in the K/V staging area while the previous tile's
+// last layer runs its out-projection and FFN.
 //
 // Roles (320 threads):
 //   warp 0      TMA producer: per layer Wv, Wk, Wq, Wo, W1, W2 (128x128 fp16
@@ -18,14 +20,16 @@
 //   warps 2..9  compute, two warps per TMEM lane quarter: lane l of warp w
 //               owns row 32*(w%4)+l of every 128-row accumulator and HALF of
 //               its columns (half = (w-2)/4). Row statistics (LayerNorm mean /
-//               variance, softmax max, softmax sums) are merged with the
-//               partner warp through shared memory and a 64-thread barrier.
+//               variance, softmax max) are merged with the partner warp
+//               through shared memory and a 64-thread barrier.
 //
 // TMEM columns: [0,128) S buffer 0 / Q; [128,256) S buffer 1 / K / FFN-in
 // accumulator; [256,384) V^T accumulator, then the per-head attention outputs
 // O (two buffers), then the fp16 A operand of the FFN GEMMs; [384,512) the
 // fp32 residual stream x of the tile, onto which the out-proj and FFN-out
 // products accumulate in place (it holds x + that product's bias before).
+// Softmax row sums are tensor-core products too (P_h . 1, see sum_col), so
+// they add exactly the fp16 weights P.V used.
 //
 // Per layer (c = compute warps, m = MMA thread):
 //   c: LN1(x) -> sA (fp16, K-major, 128B swizzle)
@@ -36,8 +40,8 @@
 //   m: S_0 -> S buffer 0, S_1 -> S buffer 1
 //   per head h (b = h % 2):
 //     c: softmax row of S_h -> P_h (fp16, <= 1) written over its own S buffer
-//     m: O_h = P_h . V_h -> O buffer b ; S_{h+2} -> S buffer b
-//     c: (while the MMAs run) ctx_{h-1} = O_{h-1} / rowsum -> sA over Q_{h-1}
+//     m: O_h = P_h . V_h -> O buffer b, l_h = P_h . 1 ; S_{h+2} -> S buffer b
+//     c: (while the MMAs run) ctx_{h-1} = O_{h-1} / l_{h-1} -> sA over Q_{h-1}
 //   m: x += ctx . Wo^T         c: LN2(x) -> TMEM A operand; x + b2 -> TMEM x
 //   m: acc = h2 . W1^T         c: g = gelu(acc + b1) -> TMEM A operand
 //   m: x += g . W2^T           c: next LN1 (x + next bo -> TMEM x) or final LN -> y
@@ -63,6 +67,7 @@ namespace tfx {
 constexpr int kFusedMaxLayers = 5;
 
 struct FusedParams {
+  CUtensorMap x_map;  // fp32 input [rows][128], 32-column boxes, 128-byte swizzle
   CUtensorMap w_qkv[kFusedMaxLayers];
   CUtensorMap w_out[kFusedMaxLayers];
   CUtensorMap w_in[kFusedMaxLayers];
@@ -77,7 +82,6 @@ struct FusedParams {
   const float* ln2_b[kFusedMaxLayers];
   const float* lnf_g;
   const float* lnf_b;
-  const float* x;
   float* y;
   const int32_t* valid_len;  // nullable: [batch] prefix lengths (padding mask)
   const uint32_t* key_bits;  // nullable: [batch][key_words] token bitmask (any padding)
@@ -105,15 +109,17 @@ constexpr int kParFloats = 1280;
 constexpr int kParBytes = (kFusedMaxLayers * kParFloats + 2 * 128) * 4;
 constexpr int kXchSlots = 2;                              // alternating pair-exchange slots
 constexpr int kXchBytes = kXchSlots * 2 * kT * 8;         // [slot][half][row] float2
-constexpr int kSumBytes = 2 * 2 * kT * 4;                 // [head parity][half][row] float
+// 16 x 64 fp16 ones (K-major, 128-byte swizzle): the B operand of the
+// products P_h . 1 that give each row's softmax sum (keys 64..127 reuse it).
+constexpr int kOnesBytes = 16 * 128;
 constexpr int kOffA = 0;
 constexpr int kOffK = kOpBytes;
 constexpr int kOffV = 2 * kOpBytes;
 constexpr int kOffW = 3 * kOpBytes;
 constexpr int kOffPar = kOffW + kWSlots * kOpBytes;
 constexpr int kOffXch = kOffPar + kParBytes;
-constexpr int kOffSum = kOffXch + kXchBytes;
-constexpr int kOffBar = kOffSum + kSumBytes;
+constexpr int kOffOnes = kOffXch + kXchBytes;
+constexpr int kOffBar = kOffOnes + kOnesBytes;
 constexpr int kSmemBytes = kOffBar + 192 + 1024;
 constexpr int kComputeWarps = 8;
 constexpr int kThreads = 32 * (2 + kComputeWarps);
@@ -130,6 +136,20 @@ constexpr int kOffK2 = kOffW + 2 * kOpBytes;
 template <int HD>
 constexpr int weight_slots() { return HD == 8 ? 2 : kWSlots; }
 static_assert(kSmemBytes <= 232448, "shared memory budget");
+static_assert(kOffOnes % 1024 == 0, "a 128-byte-swizzled operand starts on 1024 bytes");
+
+// TMEM column of head h's row sums (the N = 16 product P_h . 1; every column
+// holds the sum): after the two O buffers when there are more than two heads
+// (head_dim <= 32: O takes at most 64 columns), else in its S buffer's
+// columns [32, 48), which P_h (columns [0,32) and [64,96)) leaves free and no
+// later head reuses.
+template <int HD>
+__device__ __forceinline__ uint32_t sum_col(int h) {
+  constexpr int H = kT / HD;
+  constexpr uint32_t NPV = HD < 16 ? 16 : HD;
+  if constexpr (H > 2) return kColO + 2 * NPV + 16 * (h & 1);
+  else return ((h & 1) ? kColS1 : kColS0) + 32;
+}
 
 // Byte address of row r, columns [c, c+8) of a K-major 128x128 fp16 operand
 // stored as two 128B-swizzled 64-column blocks (the layout TMA writes with
@@ -159,6 +179,14 @@ __device__ __forceinline__ void store_q32(uint32_t base, int t, int c0, const fl
            pack_half2(v[8 * j + 2], v[8 * j + 3]), pack_half2(v[8 * j + 4], v[8 * j + 5]),
            pack_half2(v[8 * j + 6], v[8 * j + 7]));
   }
+}
+
+__device__ __forceinline__ float4 lds128f(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr));
+  return v;
 }
 
 // Row r, columns [c0, c0 + 8*N8) of a K-major operand <- fp16(v).
@@ -356,7 +384,8 @@ __device__ __forceinline__ void store_x_biased(uint32_t tl, int half, const floa
     }
     tmem_st32(tl + kColX + 64 * half + 32 * c, o);
   }
-  tmem_st_wait();
+  // No tcgen05.wait::st here: the compute warps' next hand-off to the MMA
+  // (signal) waits for every store of this thread.
 }
 
 // The out-proj and FFN-out products accumulate in place onto the residual
@@ -429,7 +458,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t sA = sbase + kOffA, sK = sbase + kOffK, sV = sbase + kOffV;
   float* par = reinterpret_cast<float*>(smem + kOffPar);  // [layer][kParFloats], then final LN
   float2* xch = reinterpret_cast<float2*>(smem + kOffXch);
-  float* psum = reinterpret_cast<float*>(smem + kOffSum);  // [head parity][half][row]
   uint64_t* w_full = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* w_empty = w_full + kWSlots;
   uint64_t* c2m = w_empty + kWSlots;  // compute -> MMA: operand ready (one arrival per warp)
@@ -445,7 +473,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   // SPLIT only, arrived on by the PEER's compute warps (one per warp):
   uint64_t* peer_ctx = m2c_k + 1;     // the peer's ctx block is in this CTA's sA
   uint64_t* peer_free = peer_ctx + 1; // the peer's QKV products no longer read its sA
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(peer_free + 1);
+  // The next tile's fp32 input has landed in the sK/sV region (TMA).
+  uint64_t* x_full = peer_free + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(x_full + 1);
   const uint32_t rank = SPLIT ? cluster_ctarank() : 0u;
   const uint32_t peer = rank ^ 1u;
   const int h0 = static_cast<int>(rank) * HL, h1 = h0 + HL;
@@ -468,6 +498,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(m2c_k, 1);
     mbar_init(peer_ctx, kComputeWarps);
     mbar_init(peer_free, kComputeWarps);
+    mbar_init(x_full, 1);
     fence_mbar_init();
   }
   grid_dep_wait();
@@ -498,6 +529,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   for (int j = threadIdx.x; j < 256; j += kThreads)
     par[kFusedMaxLayers * kParFloats + j] = j < 128 ? p.lnf_g[j] : p.lnf_b[j - 128];
+  for (int j = threadIdx.x; j < kOnesBytes / 4; j += kThreads)
+    reinterpret_cast<uint32_t*>(smem + kOffOnes)[j] = 0x3C003C00u;  // fp16 1.0 pairs
+  fence_proxy_async_smem();  // visible to the tensor core
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -516,12 +550,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < kWSlots; ++s) issued[s] = -1;
     bool ok = true;
     for (int tile = first_tile<SPLIT>(); tile < p.num_tiles && ok; tile += tile_stride<SPLIT>()) {
-      // The producer runs ahead of the compute warps (here: about one layer
-      // of the previous tile), so the tile's fp32 input is an L2 hit by the
-      // time they load it.
-      const int64_t row0 = static_cast<int64_t>(tile) * kT;
-      const int64_t nrows = p.rows - row0 < kT ? p.rows - row0 : kT;
-      bulk_prefetch_l2(p.x + row0 * kT, static_cast<uint32_t>(nrows * kT * 4));
       for (int l = 0; l < L && ok; ++l) {
         for (int c = 0; c < 6; ++c) {
           const CUtensorMap* m =
@@ -552,6 +580,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int WS = weight_slots<HD>();
     constexpr int NPV = HD < 16 ? 16 : HD;  // P.V N: a head pair at head_dim 8
     constexpr uint32_t idhd = idesc_f16_f32(128, NPV);
+    constexpr uint32_t id16 = idesc_f16_f32(128, 16);
     int slot = 0;
     uint32_t ph = 0, c2m_ph = 0;
     uint32_t mph_o[2] = {0, 0};  // this thread's view of the O-buffer barriers
@@ -566,6 +595,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint64_t dA = sdesc_k_sw128(sA), dK = sdesc_k_sw128(sK), dV = sdesc_k_sw128(sV);
     const uint64_t dK2 = sdesc_k_sw128(sbase + kOffK2);  // head_dim 8: odd heads' K copy
     const uint64_t dW0 = sdesc_k_sw128(sbase + kOffW);
+    const uint64_t dOnes = sdesc_k_sw128(sbase + kOffOnes);
     auto take_w = [&](uint64_t& w) {
       if (!mbar_wait_sleep(&w_full[slot], ph, p.err, kDevTimeoutFull)) return false;
       tc_fence_after();
@@ -598,6 +628,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_chain<HD / 16>(tmem + ((h & 1) ? kColS1 : kColS0), dA, h * HD, dK, h * HD, id128);
       mma_commit(&m2c_s[h & 1]);
     };
+    // A tile's fp32 input -> the 64 KB sK/sV region as four 32-column boxes
+    // (128-byte swizzle; rows past the batch read as zeros). The first
+    // tile's is loaded now; each next one once the last layer's attention
+    // of the current tile no longer reads K and V, so it lands during that
+    // layer's out-projection and FFN.
+    int x_loads = 0;
+    auto load_x = [&](int t) {
+      mbar_arrive_expect_tx(x_full, 4 * kT * 32 * 4);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        tma_load_2d(smem + kOffK + i * (kT * 32 * 4), &p.x_map, x_full, 32 * i, t * kT);
+      ++x_loads;
+    };
+    if (first_tile<SPLIT>() < p.num_tiles) load_x(first_tile<SPLIT>());
     bool ok = true;
     for (int tile = first_tile<SPLIT>(); tile < p.num_tiles && ok; tile += tile_stride<SPLIT>()) {
       for (int l = 0; l < L && ok; ++l) {
@@ -635,6 +679,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int k = 0; k < kT / 16; ++k)
             mma_f16_ts(tmem + kColO + (h & 1) * NPV, tmem + sb + (k < 4 ? 8 * k : 64 + 8 * (k - 4)),
                        desc_col(dVh, 16 * k), idhd, k > 0 ? 1u : 0u);
+          // Row sums of the fp16 P_h the product above used: P_h . 1.
+#pragma unroll
+          for (int k = 0; k < kT / 16; ++k)
+            mma_f16_ts(tmem + sum_col<HD>(h), tmem + sb + (k < 4 ? 8 * k : 64 + 8 * (k - 4)),
+                       desc_col(dOnes, 16 * (k & 3)), id16, k > 0 ? 1u : 0u);
           mma_commit(&m2c_o[h & 1]);
           if (h + 2 < h1) {
             // S_{h+2} reuses the columns P_h is read from: wait until P_h.V_h
@@ -651,6 +700,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           ph_peer ^= 1;
           tc_fence_after();
         }
+        // Every product reading sK and sV has completed (the compute warps
+        // saw the last head's P.V commit before completing ctx).
+        if (l == L - 1 && tile + tile_stride<SPLIT>() < p.num_tiles)
+          load_x(tile + tile_stride<SPLIT>());
         if (!(ok = take_w(w))) break;
         mma_chain<kT / 16>(tmem + kColX, dA, 0, w, 0, id128, 1u);  // x += out-proj
         release_w();
@@ -663,6 +716,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_commit(m2c_g);
       }
     }
+    // Unwinding after a timeout: no input copy may still be in flight.
+    if (x_loads > 0) mbar_wait_sleep(x_full, static_cast<uint32_t>(x_loads - 1) & 1u, nullptr, 0);
   } else if (warp >= 2) {
     // ------------------------------------------------------------- compute
     constexpr int HDH = HD / 2;  // O columns of one head handled by each warp of a pair
@@ -673,6 +728,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     Pair pr{xch, half, r, 1 + q, 0};
     uint32_t ph_g = 0, ph_v = 0, ph_k = 0, ph_s[2] = {0, 0}, ph_o[2] = {0, 0};
     uint32_t ph_pf = 0;  // SPLIT: phase of peer_free
+    uint32_t ph_x = 0;
     // Warp-uniform outcome: a timeout seen by one lane ends the whole warp.
     auto wait = [&](uint64_t* bar, uint32_t& phase) {
       const bool ok = __all_sync(0xffffffffu, mbar_wait_sleep(bar, phase, p.err, kDevTimeoutAccum));
@@ -681,6 +737,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       return ok;
     };
     auto signal = [&]() {
+      tmem_st_wait();
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
@@ -707,15 +764,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ctx_h = O_h / rowsum -> sA columns [h*HD + half*HD/2, +HD/2) (over Q_h).
     // head_dim 8: the warp of the pair whose half matches the head's parity
     // writes all 8 columns (O_h is this head's half of a 16-column product).
+    // The row sum comes from TMEM next to O (sum_col), in the same round trip.
+    auto inv_sum = [](uint32_t raw) {
+      const float l = __uint_as_float(raw);
+      return l > 0.f ? 1.0f / l : 0.f;
+    };
     auto write_ctx = [&](int h) {
-      const float l = psum[((h & 1) * 2 + 0) * kT + r] + psum[((h & 1) * 2 + 1) * kT + r];
-      const float inv = l > 0.f ? 1.0f / l : 0.f;
-      const uint64_t inv2 = f2_pack(inv, inv);
+      uint32_t lraw;
       if constexpr (HD == 8) {
         if (half == (h & 1)) {  // warp-uniform
           uint32_t o[8];
           tmem_ld8(tl + kColO + (h & 1) * 16 + (h & 1) * 8, o);
+          tmem_ld1(tl + sum_col<HD>(h), lraw);
           tmem_ld_wait();
+          const float inv = inv_sum(lraw);
+          const uint64_t inv2 = f2_pack(inv, inv);
           float v8[8];
 #pragma unroll
           for (int j = 0; j < 8; j += 2)
@@ -730,17 +793,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       if constexpr (HDH == 8) {
         uint32_t o[8];
         tmem_ld8(t_o, o);
+        tmem_ld1(tl + sum_col<HD>(h), lraw);
         tmem_ld_wait();
+        const float inv = inv_sum(lraw);
+        const uint64_t inv2 = f2_pack(inv, inv);
 #pragma unroll
         for (int j = 0; j < 8; j += 2)
           f2_unpack(f2_mul(f2_pack(__uint_as_float(o[j]), __uint_as_float(o[j + 1])), inv2),
                     v[j], v[j + 1]);
       } else {
+        tmem_ld1(tl + sum_col<HD>(h), lraw);
 #pragma unroll
         for (int c = 0; c < HDH / 16; ++c) {
           uint32_t o[16];
           tmem_ld16(t_o + 16 * c, o);
           tmem_ld_wait();
+          const float inv = inv_sum(lraw);
+          const uint64_t inv2 = f2_pack(inv, inv);
 #pragma unroll
           for (int j = 0; j < 16; j += 2)
             f2_unpack(f2_mul(f2_pack(__uint_as_float(o[j]), __uint_as_float(o[j + 1])), inv2),
@@ -772,13 +841,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       // of this warp: whole-tile sequences, no padding, below the diagonal.
       const bool plain_tile = (S == kT) && (p.valid_len == nullptr) && (p.key_bits == nullptr);
       float xv[2][32];  // this warp's 64 columns of the fp32 residual row
+      if (!(ok = wait(x_full, ph_x))) break;
       {
-        const float4* x4 = reinterpret_cast<const float4*>(p.x + grow * kT + 64 * half);
+        // Row r of box 2*half + c: 128 bytes at r*128, 16-byte chunk j at
+        // position j ^ (r % 8) (the 128-byte swizzle: conflict-free reads).
+        const uint32_t xr = sK + static_cast<uint32_t>(2 * half * (kT * 32 * 4) + r * 128);
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            const float4 t = row_ok ? __ldcs(x4 + 8 * c + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 t = lds128f(xr + c * (kT * 32 * 4) + ((j ^ (r & 7)) << 4));
             xv[c][4 * j] = t.x;
             xv[c][4 * j + 1] = t.y;
             xv[c][4 * j + 2] = t.z;
@@ -933,9 +1005,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           mx = fmaxf(mx, pr.swap(make_float2(mx, 0.f)).x);
           // All keys padding (zero-length sequence): weights exp2(-inf) = 0.
           const float mref = (mx == -INFINITY) ? 0.f : mx * sl2;
-          // Pass 2: exp2, row sum, fp16 packing in f32x2 arithmetic, from the
-          // registers pass 1 loaded (and masked).
-          uint64_t ls0 = 0, ls1 = 0;
+          // Pass 2: exp2 and fp16 packing in f32x2 arithmetic, from the
+          // registers pass 1 loaded (and masked). The row sum is the MMA's.
           const uint64_t c2 = f2_pack(sl2, sl2), negm2 = f2_pack(-mref, -mref);
           uint32_t w[32];
 #pragma unroll
@@ -952,22 +1023,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // kernel needs would only cost issue slots).
                 float a0, a1;
                 f2_unpack(arg, a0, a1);
-                const uint64_t e = f2_pack(fast_exp2(a0), fast_exp2(a1));
-                if (j & 1) ls1 = f2_add(ls1, e); else ls0 = f2_add(ls0, e);
-                float e0, e1;
-                f2_unpack(e, e0, e1);
-                w[16 * c + j] = pack_half2(e0, e1);
+                w[16 * c + j] = pack_half2(fast_exp2(a0), fast_exp2(a1));
               }
             } else {
 #pragma unroll
               for (int j = 0; j < 16; ++j) w[16 * c + j] = 0u;
             }
           }
-          float la, lb, lc, ld;
-          f2_unpack(ls0, la, lb);
-          f2_unpack(ls1, lc, ld);
-          const float sum = (la + lb) + (lc + ld);
-          psum[(b * 2 + half) * kT + r] = sum;
           tmem_st32(sb + 64 * half, w);  // P over this warp's own S columns
           tmem_st_wait();
           tc_fence_before();
@@ -981,7 +1043,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!ok || !(ok = wait(&m2c_o[(h1 - 1) & 1], ph_o[(h1 - 1) & 1]))) break;
         if (!(ok = await_peer_free())) break;
-        named_bar_sync(pr.bar_id, 64);  // partner's row sum of the last head is visible
         write_ctx(h1 - 1);
         signal();  // ctx complete
         if constexpr (SPLIT) {
@@ -1127,7 +1188,12 @@ int launch_fused_forward(const tfx_model* m, const float* x, float* y, int batch
   }
   p.lnf_g = m->final_norm_weight;
   p.lnf_b = m->final_norm_bias;
-  p.x = x;
+  const int64_t rows = static_cast<int64_t>(batch) * seq;
+  if (rows > INT32_MAX - kT)
+    return fail(TFX_ERR_UNSUPPORTED, "fused forward: %lld tokens exceed 2^31", (long long)rows);
+  if (int st = make_tmap_2d(&p.x_map, x, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, rows, kT, kT, 32, kT,
+                            CU_TENSOR_MAP_SWIZZLE_128B))
+    return st;
   p.y = y;
   p.valid_len = km.len;
   p.key_bits = km.bits;
