@@ -869,9 +869,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int l = 0; l < L; ++l) {
         const float* lp = par + l * kParFloats;
         signal();  // LN1 output in sA
-        // QKV epilogue in the order the GEMMs complete: V^T (half 0 takes the
-        // first half of the tokens of V^T row r, half 1 the second; V^T lanes
-        // are features), then K (half 1), then Q (half 0).
+        // QKV epilogue in the order the GEMMs complete, each split between the
+        // two warps of a lane quarter: V^T (half 0 takes the first half of the
+        // tokens of V^T row r, half 1 the second; V^T lanes are features), K,
+        // then Q (columns [64*half, +64), or with SPLIT 32 columns each of the
+        // CTA's 64-column block). After the last product only one TMEM round
+        // trip per warp is left.
         if (!(ok = wait(m2c_v, ph_v))) break;
         {
           const float bv = lp[kPQkv + 256 + r];  // V bias of feature r
@@ -892,35 +895,33 @@ __global__ void __launch_bounds__(kThreads, 1)
                       v[j], v[j + 1]);
           store_row<4>(sV, r, 64 * half + 32, v);
         }
-        if (!(ok = wait(m2c_k, ph_k))) break;
-        if (half == 0 && !(ok = wait(m2c_g, ph_g))) break;
-#pragma unroll 1
-        for (int i = 0; i < 4; i += 2) {  // Q chunks 0..3 (half 0) or K chunks 4..7 (half 1)
-          // SPLIT: only the 64-column block of this CTA's heads.
-          if (SPLIT && i != 2 * static_cast<int>(rank)) continue;
-          uint32_t ra[32], rb[32];
-          tmem_ld32(tl + 32 * (4 * half + i), ra);
-          tmem_ld32(tl + 32 * (4 * half + i) + 32, rb);
+        // 32-column chunks c0 .. c0+NC-1 of Q (TMEM/bias chunk q0 = 0) or K (4).
+        constexpr int NC = SPLIT ? 1 : 2;
+        const int c0 = SPLIT ? 2 * static_cast<int>(rank) + half : 2 * half;
+        auto qk_epilogue = [&](int q0) {
+          uint32_t ra[NC][32];
+#pragma unroll
+          for (int n = 0; n < NC; ++n) tmem_ld32(tl + 32 * (q0 + c0 + n), ra[n]);
           tmem_ld_wait();
-          float v[2][32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            v[0][j] = __uint_as_float(ra[j]);
-            v[1][j] = __uint_as_float(rb[j]);
-          }
+          for (int n = 0; n < NC; ++n) {
+            float v[32];
 #pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            add_bias32(v[u], lp + kPQkv + 32 * (4 * half + i + u));
-            if (half == 0)
-              store_q32<HD>(sA, r, 32 * (i + u), v[u]);
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(ra[n][j]);
+            add_bias32(v, lp + kPQkv + 32 * (q0 + c0 + n));
+            if (q0 == 0)
+              store_q32<HD>(sA, r, 32 * (c0 + n), v);
+            else if constexpr (HD == 8)
+              store_k_split(sK, sbase + kOffK2, r, 32 * (c0 + n), v);
             else
-              if constexpr (HD == 8)
-                store_k_split(sK, sbase + kOffK2, r, 32 * (i + u), v[u]);
-              else
-                store_row<4>(sK, r, 32 * (i + u), v[u]);
+              store_row<4>(sK, r, 32 * (c0 + n), v);
           }
-        }
-        if (half == 1 && !(ok = wait(m2c_g, ph_g))) break;  // keeps this warp's m2c_g phase
+        };
+        if (!(ok = wait(m2c_k, ph_k))) break;
+        qk_epilogue(4);
+        // Q goes over h in sA, which all three products read: after the last.
+        if (!(ok = wait(m2c_g, ph_g))) break;
+        qk_epilogue(0);
         signal();
         if constexpr (SPLIT) {
           // This CTA's QKV products are complete (m2c_g): the block of sA the
