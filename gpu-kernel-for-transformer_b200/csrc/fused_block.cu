@@ -256,8 +256,21 @@ __device__ __forceinline__ void mma_chain(uint32_t d, uint64_t a_desc, int a_col
 // v[j] += b[j] for j in [0, 32) (b in shared memory; every lane reads the
 // same address). The elementwise helpers below work on column pairs with
 // f32x2 arithmetic: half the instructions, the same rounding per element.
+//
+// Per-column parameters (biases, LayerNorm gamma and beta) are read from
+// shared memory in batches of N float4, all issued before the first is used
+// (volatile loads stay together): one load latency per batch. Left to the
+// compiler at the 168-register cap, each load waited for its own use.
+template <int N>
+__device__ __forceinline__ void lds_batch(const float* p, float4 (&o)[N]) {
+  const uint32_t a = smem_u32(p);
+#pragma unroll
+  for (int k = 0; k < N; ++k) o[k] = lds128f(a + 16 * k);
+}
+
 __device__ __forceinline__ void add_bias32(float (&v)[32], const float* b) {
-  const float4* b4 = reinterpret_cast<const float4*>(b);
+  float4 b4[8];
+  lds_batch<8>(b, b4);
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const float4 t = b4[j];
@@ -334,13 +347,17 @@ __device__ __forceinline__ void ln_apply(const float (&x)[2][32], float mean, fl
   // (x - mean) * rstd as x * rstd + (-mean * rstd): two FMAs per pair.
   const uint64_t rstd2 = f2_pack(rstd, rstd), nmr2 = f2_pack(-mean * rstd, -mean * rstd);
 #pragma unroll
-  for (int c = 0; c < 2; ++c) {
-    const int col = 64 * half + 32 * c;
-    const float4* g4 = reinterpret_cast<const float4*>(g + col);
-    const float4* b4 = reinterpret_cast<const float4*>(b + col);
+  for (int c = 0; c < 2; ++c)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float4 gg = g4[j], bb = b4[j];
+  for (int jb = 0; jb < 8; jb += 4) {
+    const int col = 64 * half + 32 * c + 4 * jb;
+    float4 g4[4], b4[4];
+    lds_batch<4>(g + col, g4);
+    lds_batch<4>(b + col, b4);
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+      const int j = jb + jj;
+      const float4 gg = g4[jj], bb = b4[jj];
       const uint64_t lo = f2_fma(f2_fma(f2_pack(x[c][4 * j], x[c][4 * j + 1]), rstd2, nmr2),
                                  f2_pack(gg.x, gg.y), f2_pack(bb.x, bb.y));
       const uint64_t hi = f2_fma(f2_fma(f2_pack(x[c][4 * j + 2], x[c][4 * j + 3]), rstd2, nmr2),
@@ -369,7 +386,8 @@ __device__ __forceinline__ void store_x_biased(uint32_t tl, int half, const floa
                                                const float (&x)[2][32]) {
 #pragma unroll
   for (int c = 0; c < 2; ++c) {
-    const float4* b4 = reinterpret_cast<const float4*>(bias + 64 * half + 32 * c);
+    float4 b4[8];
+    lds_batch<8>(bias + 64 * half + 32 * c, b4);
     uint32_t o[32];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
