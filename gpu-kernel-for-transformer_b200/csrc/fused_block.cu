@@ -20,16 +20,14 @@
 //   warps 2..9  compute, two warps per TMEM lane quarter: lane l of warp w
 //               owns row 32*(w%4)+l of every 128-row accumulator and HALF of
 //               its columns (half = (w-2)/4). Row statistics (LayerNorm mean /
-//               variance, softmax max) are merged with the partner warp
-//               through shared memory and a 64-thread barrier.
+//               variance, softmax max, softmax sums) are merged with the
+//               partner warp through shared memory and a 64-thread barrier.
 //
 // TMEM columns: [0,128) S buffer 0 / Q; [128,256) S buffer 1 / K / FFN-in
 // accumulator; [256,384) V^T accumulator, then the per-head attention outputs
 // O (two buffers), then the fp16 A operand of the FFN GEMMs; [384,512) the
 // fp32 residual stream x of the tile, onto which the out-proj and FFN-out
 // products accumulate in place (it holds x + that product's bias before).
-// Softmax row sums are tensor-core products too (P_h . 1, see sum_col), so
-// they add exactly the fp16 weights P.V used.
 //
 // Per layer (c = compute warps, m = MMA thread):
 //   c: LN1(x) -> sA (fp16, K-major, 128B swizzle)
@@ -40,7 +38,7 @@
 //   m: S_0 -> S buffer 0, S_1 -> S buffer 1
 //   per head h (b = h % 2):
 //     c: softmax row of S_h -> P_h (fp16, <= 1) written over its own S buffer
-//     m: O_h = P_h . V_h -> O buffer b, l_h = P_h . 1 ; S_{h+2} -> S buffer b
+//     m: O_h = P_h . V_h -> O buffer b ; S_{h+2} -> S buffer b
 //     c: (while the MMAs run) ctx_{h-1} = O_{h-1} / l_{h-1} -> sA over Q_{h-1}
 //   m: x += ctx . Wo^T         c: LN2(x) -> TMEM A operand; x + b2 -> TMEM x
 //   m: acc = h2 . W1^T         c: g = gelu(acc + b1) -> TMEM A operand
@@ -109,17 +107,15 @@ constexpr int kParFloats = 1280;
 constexpr int kParBytes = (kFusedMaxLayers * kParFloats + 2 * 128) * 4;
 constexpr int kXchSlots = 2;                              // alternating pair-exchange slots
 constexpr int kXchBytes = kXchSlots * 2 * kT * 8;         // [slot][half][row] float2
-// 16 x 64 fp16 ones (K-major, 128-byte swizzle): the B operand of the
-// products P_h . 1 that give each row's softmax sum (keys 64..127 reuse it).
-constexpr int kOnesBytes = 16 * 128;
+constexpr int kSumBytes = 2 * 2 * kT * 4;                 // [head parity][half][row] float
 constexpr int kOffA = 0;
 constexpr int kOffK = kOpBytes;
 constexpr int kOffV = 2 * kOpBytes;
 constexpr int kOffW = 3 * kOpBytes;
 constexpr int kOffPar = kOffW + kWSlots * kOpBytes;
 constexpr int kOffXch = kOffPar + kParBytes;
-constexpr int kOffOnes = kOffXch + kXchBytes;
-constexpr int kOffBar = kOffOnes + kOnesBytes;
+constexpr int kOffSum = kOffXch + kXchBytes;
+constexpr int kOffBar = kOffSum + kSumBytes;
 constexpr int kSmemBytes = kOffBar + 192 + 1024;
 constexpr int kComputeWarps = 8;
 constexpr int kThreads = 32 * (2 + kComputeWarps);
@@ -136,20 +132,7 @@ constexpr int kOffK2 = kOffW + 2 * kOpBytes;
 template <int HD>
 constexpr int weight_slots() { return HD == 8 ? 2 : kWSlots; }
 static_assert(kSmemBytes <= 232448, "shared memory budget");
-static_assert(kOffOnes % 1024 == 0, "a 128-byte-swizzled operand starts on 1024 bytes");
 
-// TMEM column of head h's row sums (the N = 16 product P_h . 1; every column
-// holds the sum): after the two O buffers when there are more than two heads
-// (head_dim <= 32: O takes at most 64 columns), else in its S buffer's
-// columns [32, 48), which P_h (columns [0,32) and [64,96)) leaves free and no
-// later head reuses.
-template <int HD>
-__device__ __forceinline__ uint32_t sum_col(int h) {
-  constexpr int H = kT / HD;
-  constexpr uint32_t NPV = HD < 16 ? 16 : HD;
-  if constexpr (H > 2) return kColO + 2 * NPV + 16 * (h & 1);
-  else return ((h & 1) ? kColS1 : kColS0) + 32;
-}
 
 // Byte address of row r, columns [c, c+8) of a K-major 128x128 fp16 operand
 // stored as two 128B-swizzled 64-column blocks (the layout TMA writes with
@@ -476,6 +459,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t sA = sbase + kOffA, sK = sbase + kOffK, sV = sbase + kOffV;
   float* par = reinterpret_cast<float*>(smem + kOffPar);  // [layer][kParFloats], then final LN
   float2* xch = reinterpret_cast<float2*>(smem + kOffXch);
+  float* psum = reinterpret_cast<float*>(smem + kOffSum);
   uint64_t* w_full = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* w_empty = w_full + kWSlots;
   uint64_t* c2m = w_empty + kWSlots;  // compute -> MMA: operand ready (one arrival per warp)
@@ -547,8 +531,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   for (int j = threadIdx.x; j < 256; j += kThreads)
     par[kFusedMaxLayers * kParFloats + j] = j < 128 ? p.lnf_g[j] : p.lnf_b[j - 128];
-  for (int j = threadIdx.x; j < kOnesBytes / 4; j += kThreads)
-    reinterpret_cast<uint32_t*>(smem + kOffOnes)[j] = 0x3C003C00u;  // fp16 1.0 pairs
   fence_proxy_async_smem();  // visible to the tensor core
   tc_fence_before();
   __syncthreads();
@@ -598,7 +580,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int WS = weight_slots<HD>();
     constexpr int NPV = HD < 16 ? 16 : HD;  // P.V N: a head pair at head_dim 8
     constexpr uint32_t idhd = idesc_f16_f32(128, NPV);
-    constexpr uint32_t id16 = idesc_f16_f32(128, 16);
     int slot = 0;
     uint32_t ph = 0, c2m_ph = 0;
     uint32_t mph_o[2] = {0, 0};  // this thread's view of the O-buffer barriers
@@ -613,7 +594,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint64_t dA = sdesc_k_sw128(sA), dK = sdesc_k_sw128(sK), dV = sdesc_k_sw128(sV);
     const uint64_t dK2 = sdesc_k_sw128(sbase + kOffK2);  // head_dim 8: odd heads' K copy
     const uint64_t dW0 = sdesc_k_sw128(sbase + kOffW);
-    const uint64_t dOnes = sdesc_k_sw128(sbase + kOffOnes);
     auto take_w = [&](uint64_t& w) {
       if (!mbar_wait_sleep(&w_full[slot], ph, p.err, kDevTimeoutFull)) return false;
       tc_fence_after();
@@ -697,11 +677,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int k = 0; k < kT / 16; ++k)
             mma_f16_ts(tmem + kColO + (h & 1) * NPV, tmem + sb + (k < 4 ? 8 * k : 64 + 8 * (k - 4)),
                        desc_col(dVh, 16 * k), idhd, k > 0 ? 1u : 0u);
-          // Row sums of the fp16 P_h the product above used: P_h . 1.
-#pragma unroll
-          for (int k = 0; k < kT / 16; ++k)
-            mma_f16_ts(tmem + sum_col<HD>(h), tmem + sb + (k < 4 ? 8 * k : 64 + 8 * (k - 4)),
-                       desc_col(dOnes, 16 * (k & 3)), id16, k > 0 ? 1u : 0u);
           mma_commit(&m2c_o[h & 1]);
           if (h + 2 < h1) {
             // S_{h+2} reuses the columns P_h is read from: wait until P_h.V_h
@@ -782,20 +757,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ctx_h = O_h / rowsum -> sA columns [h*HD + half*HD/2, +HD/2) (over Q_h).
     // head_dim 8: the warp of the pair whose half matches the head's parity
     // writes all 8 columns (O_h is this head's half of a 16-column product).
-    // The row sum comes from TMEM next to O (sum_col), in the same round trip.
-    auto inv_sum = [](uint32_t raw) {
-      const float l = __uint_as_float(raw);
-      return l > 0.f ? 1.0f / l : 0.f;
-    };
     auto write_ctx = [&](int h) {
-      uint32_t lraw;
+      // Row sum of head h: the pair's two halves (inverted after the TMEM load).
+      const float l = psum[((h & 1) * 2 + 0) * kT + r] + psum[((h & 1) * 2 + 1) * kT + r];
       if constexpr (HD == 8) {
         if (half == (h & 1)) {  // warp-uniform
           uint32_t o[8];
           tmem_ld8(tl + kColO + (h & 1) * 16 + (h & 1) * 8, o);
-          tmem_ld1(tl + sum_col<HD>(h), lraw);
           tmem_ld_wait();
-          const float inv = inv_sum(lraw);
+          const float inv = l > 0.f ? 1.0f / l : 0.f;
           const uint64_t inv2 = f2_pack(inv, inv);
           float v8[8];
 #pragma unroll
@@ -811,22 +781,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       if constexpr (HDH == 8) {
         uint32_t o[8];
         tmem_ld8(t_o, o);
-        tmem_ld1(tl + sum_col<HD>(h), lraw);
         tmem_ld_wait();
-        const float inv = inv_sum(lraw);
+        const float inv = l > 0.f ? 1.0f / l : 0.f;
         const uint64_t inv2 = f2_pack(inv, inv);
 #pragma unroll
         for (int j = 0; j < 8; j += 2)
           f2_unpack(f2_mul(f2_pack(__uint_as_float(o[j]), __uint_as_float(o[j + 1])), inv2),
                     v[j], v[j + 1]);
       } else {
-        tmem_ld1(tl + sum_col<HD>(h), lraw);
 #pragma unroll
         for (int c = 0; c < HDH / 16; ++c) {
           uint32_t o[16];
           tmem_ld16(t_o + 16 * c, o);
           tmem_ld_wait();
-          const float inv = inv_sum(lraw);
+          const float inv = l > 0.f ? 1.0f / l : 0.f;
           const uint64_t inv2 = f2_pack(inv, inv);
 #pragma unroll
           for (int j = 0; j < 16; j += 2)
@@ -1024,8 +992,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           mx = fmaxf(mx, pr.swap(make_float2(mx, 0.f)).x);
           // All keys padding (zero-length sequence): weights exp2(-inf) = 0.
           const float mref = (mx == -INFINITY) ? 0.f : mx * sl2;
-          // Pass 2: exp2 and fp16 packing in f32x2 arithmetic, from the
-          // registers pass 1 loaded (and masked). The row sum is the MMA's.
+          // Pass 2: exp2, row sum, fp16 packing in f32x2 arithmetic, from the
+          // registers pass 1 loaded (and masked).
+          uint64_t ls0 = 0, ls1 = 0;
           const uint64_t c2 = f2_pack(sl2, sl2), negm2 = f2_pack(-mref, -mref);
           uint32_t w[32];
 #pragma unroll
@@ -1042,12 +1011,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // kernel needs would only cost issue slots).
                 float a0, a1;
                 f2_unpack(arg, a0, a1);
-                w[16 * c + j] = pack_half2(fast_exp2(a0), fast_exp2(a1));
+                const uint64_t e = f2_pack(fast_exp2(a0), fast_exp2(a1));
+                if (j & 1) ls1 = f2_add(ls1, e); else ls0 = f2_add(ls0, e);
+                float e0, e1;
+                f2_unpack(e, e0, e1);
+                w[16 * c + j] = pack_half2(e0, e1);
               }
             } else {
 #pragma unroll
               for (int j = 0; j < 16; ++j) w[16 * c + j] = 0u;
             }
+          }
+          {
+            float la, lb, lc, ld;
+            f2_unpack(ls0, la, lb);
+            f2_unpack(ls1, lc, ld);
+            psum[(b * 2 + half) * kT + r] = (la + lb) + (lc + ld);
           }
           tmem_st32(sb + 64 * half, w);  // P over this warp's own S columns
           tmem_st_wait();
@@ -1062,6 +1041,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!ok || !(ok = wait(&m2c_o[(h1 - 1) & 1], ph_o[(h1 - 1) & 1]))) break;
         if (!(ok = await_peer_free())) break;
+        named_bar_sync(pr.bar_id, 64);  // partner's row sum of the last head is visible
         write_ctx(h1 - 1);
         signal();  // ctx complete
         if constexpr (SPLIT) {
