@@ -445,30 +445,31 @@ __device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
 }
 
 // Exact-erf GELU of a pair, x * Phi(x) = x/2 * (1 + erf(x / sqrt 2)), on the
-// FMA pipe only (no MUFU). erf(z) = zc * Q(t): zc = z clamped to [-3.5, 3.5]
-// (1 - erf(3.5) = 7.4e-7) and t = zc^2 * 2/3.5^2 - 1 in [-1, 1], where the
-// monomial basis is well conditioned for fp32. Q (degree 9) is a fit
-// computed for this file: Lawson's iteratively reweighted least squares
-// towards the minimax absolute error of erf on [0, 3.5]. Evaluated in fp32:
+// FMA pipe only (no MUFU). With z = x / sqrt 2: erf(z) = zc * Q(t), zc = z
+// clamped to [-3.5, 3.5] (1 - erf(3.5) = 7.4e-7) and t = zc^2 * 2/3.5^2 - 1 in
+// [-1, 1], where the monomial basis is well conditioned for fp32. Q (degree
+// 9) is a fit computed for this file: Lawson's iteratively reweighted least
+// squares towards the minimax absolute error of erf on [0, 3.5]. Evaluated
+// as x * (1/2 + xc * Q'(t)) with xc = x clamped to +-3.5 sqrt 2, t = xc^2 /
+// 3.5^2 - 1 and Q' = Q / (2 sqrt 2) (13 paired FMA-pipe operations). In fp32:
 // |erf error| <= 2.6e-5, so |GELU error| <= 1.3e-5 * |x| (the fp16 the result
 // is stored in rounds by 2.4e-4 relative: 6.5e-5 against 1.2e-3 at |x| = 5).
 __device__ __forceinline__ uint64_t gelu_poly_f2(uint64_t x) {
-  const uint64_t z = f2_mul(x, f2_pack(0.70710678118654752f, 0.70710678118654752f));
-  float z0, z1;
-  f2_unpack(z, z0, z1);
-  const uint64_t zc = f2_pack(fminf(fmaxf(z0, -3.5f), 3.5f), fminf(fmaxf(z1, -3.5f), 3.5f));
-  const uint64_t t = f2_fma(zc, f2_mul(zc, f2_pack(0.16326530277729034f, 0.16326530277729034f)),
+  constexpr float kClamp = 4.949747562408447f;  // 3.5 * sqrt 2
+  float x0, x1;
+  f2_unpack(x, x0, x1);
+  const uint64_t xc = f2_pack(fminf(fmaxf(x0, -kClamp), kClamp), fminf(fmaxf(x1, -kClamp), kClamp));
+  const uint64_t t = f2_fma(xc, f2_mul(xc, f2_pack(0.08163265138864517f, 0.08163265138864517f)),
                             f2_pack(-1.0f, -1.0f));
-  constexpr float kQ[10] = {0.40388262271881104f,  -0.2006736695766449f,
-                            0.14621411263942719f,  -0.1148807480931282f,
-                            0.0930648073554039f,   -0.0648399367928505f,
-                            0.031268078833818436f, -0.026276228949427605f,
-                            0.03253420069813728f,  -0.014586295001208782f};
+  constexpr float kQ[10] = {0.14279407262802124f,  -0.07094885408878326f,
+                            0.05169449374079704f,  -0.0406164787709713f,
+                            0.03290337696671486f,  -0.022924380376935005f,
+                            0.011054934933781624f, -0.009290049783885479f,
+                            0.011502576991915703f, -0.005157033912837505f};
   uint64_t p = f2_pack(kQ[9], kQ[9]);
 #pragma unroll
   for (int k = 8; k >= 0; --k) p = f2_fma(p, t, f2_pack(kQ[k], kQ[k]));
-  const uint64_t h = f2_mul(x, f2_pack(0.5f, 0.5f));
-  return f2_fma(h, f2_mul(zc, p), h);
+  return f2_mul(x, f2_fma(xc, p, f2_pack(0.5f, 0.5f)));
 }
 
 // max(a, b, c) in one instruction (sm_100 three-input max).
