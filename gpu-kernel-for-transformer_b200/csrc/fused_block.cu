@@ -446,7 +446,11 @@ __device__ __forceinline__ int tile_stride() {
 // before the out-projection. Used when the batch has at most half as many
 // tiles as the GPU has SMs (c1, c4), where a tile's latency, not the SMs'
 // throughput, sets the time.
-template <int HD, bool SPLIT>
+//
+// PLAIN: seq_len = 128 and no padding mask (the benchmark shapes): each tile
+// is one whole sequence with every token valid, so the per-tile sequence and
+// mask bookkeeping is compile-time and holds no registers.
+template <int HD, bool SPLIT, bool PLAIN>
 __global__ void __launch_bounds__(kThreads, 1)
     fused_forward_kernel(const __grid_constant__ FusedParams p) {
   constexpr int H = kT / HD;
@@ -736,7 +740,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(c2m);
     };
-    const int S = p.seq;
+    const int S = PLAIN ? kT : p.seq;
     // Per head parity (odd heads: reversed rows): the query token of this
     // lane's S row, its key range (own sequence; causal) and the
     // warp-uniform range of 32-key chunks that can hold a valid key.
@@ -808,24 +812,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int tile = first_tile<SPLIT>(); tile < p.num_tiles && ok; tile += tile_stride<SPLIT>()) {
       const int64_t grow = static_cast<int64_t>(tile) * kT + r;
-      const bool row_ok = grow < p.rows;
+      const bool row_ok = PLAIN || grow < p.rows;
       const int64_t gt1 = static_cast<int64_t>(tile) * kT + tok1;
-      const int len = (p.valid_len != nullptr && row_ok) ? p.valid_len[grow / S] : S;
-      const int len1 = (p.valid_len != nullptr && gt1 < p.rows) ? p.valid_len[gt1 / S] : S;
+      const int len = (!PLAIN && p.valid_len != nullptr && row_ok) ? p.valid_len[grow / S] : S;
+      const int len1 = (!PLAIN && p.valid_len != nullptr && gt1 < p.rows) ? p.valid_len[gt1 / S] : S;
       const int key_hi0 = min(khn0, seq_lo0 + len - 1);  // padded keys masked
       const int key_hi1 = min(khn1, seq_lo1 + len1 - 1);
       bool row_valid = (r - seq_lo0) < len;  // not a padded token
       // Key bitmask: the words of this warp's two key chunks (all ones
       // without one) and this lane's own token bit.
       uint32_t kw0 = 0xffffffffu, kw1 = 0xffffffffu;
-      if (p.key_bits != nullptr) {
+      if (!PLAIN && p.key_bits != nullptr) {
         kw0 = tile_key_word(p, tile, 2 * half);
         kw1 = tile_key_word(p, tile, 2 * half + 1);
         row_valid = (tile_key_word(p, tile, q) >> lane) & 1u;
       }
       // A chunk needs no masking when every key in it is valid for every row
       // of this warp: whole-tile sequences, no padding, below the diagonal.
-      const bool plain_tile = (S == kT) && (p.valid_len == nullptr) && (p.key_bits == nullptr);
+      const bool plain_tile = PLAIN || ((S == kT) && (p.valid_len == nullptr) && (p.key_bits == nullptr));
       float xv[2][32];  // this warp's 64 columns of the fp32 residual row
       if (!(ok = wait(x_full, ph_x))) break;
       {
@@ -970,7 +974,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (plain_tile) {
 #pragma unroll
                 for (int j = 0; j < 32; ++j) sc[j] = j <= jhi ? sc[j] : -INFINITY;
-              } else if (p.key_bits != nullptr) {
+              } else if (!PLAIN && p.key_bits != nullptr) {
                 const uint32_t cw = c ? kw1 : kw0;
 #pragma unroll
                 for (int j = 0; j < 32; ++j)
@@ -1215,20 +1219,29 @@ int launch_fused_forward(const tfx_model* m, const float* x, float* y, int batch
   // Few tiles (at most one per two SMs): two CTAs per tile, heads split.
   const bool split = hd < kT && 2 * p.num_tiles <= sms;
   const int grid = split ? 2 * p.num_tiles : (p.num_tiles < sms ? p.num_tiles : sms);
+  const bool plain = seq == kT && !km.any();
   int st = TFX_OK;
+  // One CTA per tile (or a CTA pair), with or without the mask bookkeeping.
+#define TFX_FUSED_LAUNCH(HDV, SPL, PLN)                                                         \
+  do {                                                                                          \
+    static int done[kMaxDevices] = {0};                                                         \
+    if (SPL) {                                                                                  \
+      st = launch_split(fused_forward_kernel<HDV, SPL, PLN>, grid, p, stream, done);            \
+    } else {                                                                                    \
+      st = ensure_smem(reinterpret_cast<const void*>(fused_forward_kernel<HDV, SPL, PLN>),      \
+                       kSmemBytes, done);                                                       \
+      if (st == TFX_OK)                                                                         \
+        launch_pdl(fused_forward_kernel<HDV, SPL, PLN>, dim3(grid), dim3(kThreads), kSmemBytes, \
+                   stream, p);                                                                  \
+    }                                                                                           \
+  } while (0)
 #define TFX_FUSED_CASE(HDV)                                                                     \
   case HDV: {                                                                                   \
-    if (split && HDV < kT) {                                                                    \
-      static int done_s[kMaxDevices] = {0};                                                     \
-      st = launch_split(fused_forward_kernel<HDV, (HDV < kT)>, grid, p, stream, done_s);        \
-    } else {                                                                                    \
-      static int done[kMaxDevices] = {0};                                                       \
-      st = ensure_smem(reinterpret_cast<const void*>(fused_forward_kernel<HDV, false>),         \
-                       kSmemBytes, done);                                                       \
-      if (st != TFX_OK) return st;                                                              \
-      launch_pdl(fused_forward_kernel<HDV, false>, dim3(grid), dim3(kThreads), kSmemBytes,      \
-                 stream, p);                                                                    \
-    }                                                                                           \
+    constexpr bool kCanSplit = HDV < kT;                                                        \
+    if (split && plain) TFX_FUSED_LAUNCH(HDV, kCanSplit, true);                                 \
+    else if (split) TFX_FUSED_LAUNCH(HDV, kCanSplit, false);                                    \
+    else if (plain) TFX_FUSED_LAUNCH(HDV, false, true);                                         \
+    else TFX_FUSED_LAUNCH(HDV, false, false);                                                   \
     if (st != TFX_OK) return st;                                                                \
     break;                                                                                      \
   }
@@ -1241,6 +1254,7 @@ int launch_fused_forward(const tfx_model* m, const float* x, float* y, int batch
     default:
       return fail(TFX_ERR_UNSUPPORTED, "fused forward: head_dim %d", hd);
   }
+#undef TFX_FUSED_LAUNCH
 #undef TFX_FUSED_CASE
   return check_launch("fused_forward_kernel");
 }
