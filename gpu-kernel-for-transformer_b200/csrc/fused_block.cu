@@ -723,13 +723,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = q * 32 + lane;
     const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16);
     Pair pr{xch, half, r, 1 + q, 0};
-    uint32_t ph_g = 0, ph_v = 0, ph_k = 0, ph_s[2] = {0, 0}, ph_o[2] = {0, 0};
-    uint32_t ph_pf = 0;  // SPLIT: phase of peer_free
-    uint32_t ph_x = 0;
+    // Phase bits of this warp's barrier waits, one register for all of them.
+    enum : int { kPhG = 0, kPhV = 1, kPhK = 2, kPhS = 3, kPhO = 5, kPhPf = 7, kPhX = 8 };
+    uint32_t phs = 0;
     // Warp-uniform outcome: a timeout seen by one lane ends the whole warp.
-    auto wait = [&](uint64_t* bar, uint32_t& phase) {
-      const bool ok = __all_sync(0xffffffffu, mbar_wait_sleep(bar, phase, p.err, kDevTimeoutAccum));
-      phase ^= 1;
+    auto wait = [&](uint64_t* bar, int bit) {
+      const bool ok = __all_sync(0xffffffffu, mbar_wait_sleep(bar, (phs >> bit) & 1u, p.err,
+                                                              kDevTimeoutAccum));
+      phs ^= 1u << bit;
       tc_fence_after();
       return ok;
     };
@@ -831,7 +832,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // of this warp: whole-tile sequences, no padding, below the diagonal.
       const bool plain_tile = PLAIN || ((S == kT) && (p.valid_len == nullptr) && (p.key_bits == nullptr));
       float xv[2][32];  // this warp's 64 columns of the fp32 residual row
-      if (!(ok = wait(x_full, ph_x))) break;
+      if (!(ok = wait(x_full, kPhX))) break;
       {
         // Row r of box 2*half + c: 128 bytes at r*128, 16-byte chunk j at
         // position j ^ (r % 8) (the 128-byte swizzle: conflict-free reads).
@@ -865,7 +866,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // then Q (columns [64*half, +64), or with SPLIT 32 columns each of the
         // CTA's 64-column block). After the last product only one TMEM round
         // trip per warp is left.
-        if (!(ok = wait(m2c_v, ph_v))) break;
+        if (!(ok = wait(m2c_v, kPhV))) break;
         {
           const float bv = lp[kPQkv + 256 + r];  // V bias of feature r
           const uint64_t bv2 = f2_pack(bv, bv);
@@ -907,10 +908,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               store_row<4>(sK, r, 32 * (c0 + n), v);
           }
         };
-        if (!(ok = wait(m2c_k, ph_k))) break;
+        if (!(ok = wait(m2c_k, kPhK))) break;
         qk_epilogue(4);
         // Q goes over h in sA, which all three products read: after the last.
-        if (!(ok = wait(m2c_g, ph_g))) break;
+        if (!(ok = wait(m2c_g, kPhG))) break;
         qk_epilogue(0);
         signal();
         if constexpr (SPLIT) {
@@ -924,8 +925,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (peer_free_seen) return true;
           peer_free_seen = true;
           const bool r2 =
-              __all_sync(0xffffffffu, mbar_wait_cluster(peer_free, ph_pf, p.err, kDevTimeoutOther));
-          ph_pf ^= 1;
+              __all_sync(0xffffffffu, mbar_wait_cluster(peer_free, (phs >> kPhPf) & 1u, p.err,
+                                                        kDevTimeoutOther));
+          phs ^= 1u << kPhPf;
           return r2;
         };
         // Attention, double-buffered over heads.
@@ -933,7 +935,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int h = h0; h < h1; ++h) {
           const int b = h & 1;
           const uint32_t sb = tl + (b ? kColS1 : kColS0);
-          if (!(ok = wait(&m2c_s[b], ph_s[b]))) break;
+          if (!(ok = wait(&m2c_s[b], kPhS + b))) break;
           // Odd heads use the reversed-row key ranges.
           const int lo_e = b ? ch_lo1 : ch_lo0, hi_e = b ? ch_hi1 : ch_hi0;
           const int qq_e = b ? qq1 : qq0;
@@ -1043,12 +1045,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&c2m_p[b]);
           if (h > h0) {  // overlap: finish the previous head while P.V runs
-            if (!(ok = wait(&m2c_o[b ^ 1], ph_o[b ^ 1]))) break;
+            if (!(ok = wait(&m2c_o[b ^ 1], kPhO + (b ^ 1)))) break;
             if (!(ok = await_peer_free())) break;
             write_ctx(h - 1);
           }
         }
-        if (!ok || !(ok = wait(&m2c_o[(h1 - 1) & 1], ph_o[(h1 - 1) & 1]))) break;
+        if (!ok || !(ok = wait(&m2c_o[(h1 - 1) & 1], kPhO + ((h1 - 1) & 1)))) break;
         if (!(ok = await_peer_free())) break;
         named_bar_sync(pr.bar_id, 64);  // partner's row sum of the last head is visible
         write_ctx(h1 - 1);
@@ -1059,7 +1061,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(peer_ctx), peer));
         }
-        if (!(ok = wait(m2c_g, ph_g))) break;  // out-proj accumulator
+        if (!(ok = wait(m2c_g, kPhG))) break;  // out-proj accumulator
         {
           float mean, rstd, v[2][32];
           residual_read(tl, half, lp + kPFo, xv);  // x + out-proj; store x + b2
@@ -1068,7 +1070,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           store_a_tmem(tl, half, v);
         }
         signal();
-        if (!(ok = wait(m2c_g, ph_g))) break;  // FFN-in accumulator
+        if (!(ok = wait(m2c_g, kPhG))) break;  // FFN-in accumulator
         {
           float v[2][32];
           {
@@ -1093,7 +1095,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           store_a_tmem(tl, half, v);
         }
         signal();
-        if (!(ok = wait(m2c_g, ph_g))) break;  // FFN-out accumulator
+        if (!(ok = wait(m2c_g, kPhG))) break;  // FFN-out accumulator
         {
           float mean, rstd, v[2][32];
           residual_read(tl, half, l + 1 < L ? lp + kParFloats + kPOut : nullptr, xv);
