@@ -734,9 +734,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       return ok;
     };
-    auto signal = [&]() {
+    // smem: the phase wrote an MMA operand to shared memory (generic-proxy
+    // stores the tensor core must see); TMEM-only phases skip that fence.
+    auto signal = [&](bool smem = true) {
       tmem_st_wait();
-      fence_proxy_async_smem();
+      if (smem) fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(c2m);
@@ -1069,7 +1071,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ln_apply(xv, mean, rstd, lp + kPLn2g, lp + kPLn2b, half, v);
           store_a_tmem(tl, half, v);
         }
-        signal();
+        signal(false);  // TMEM A operand only
         if (!(ok = wait(m2c_g, kPhG))) break;  // FFN-in accumulator
         {
           float v[2][32];
@@ -1094,7 +1096,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           store_a_tmem(tl, half, v);
         }
-        signal();
+        signal(false);  // TMEM A operand only
         if (!(ok = wait(m2c_g, kPhG))) break;  // FFN-out accumulator
         {
           float mean, rstd, v[2][32];
