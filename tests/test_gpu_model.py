@@ -298,3 +298,29 @@ def test_cta_pair_mode_equals_single_cta_mode(pkg, dev, heads, seq):
         y_big = cand(x.to(dev))
         y_small = cand(x[:small_b].contiguous().to(dev))
     assert torch.equal(y_small, y_big[:small_b])
+
+
+@pytest.mark.parametrize("heads,batch", [(4, 8), (4, 400), (16, 64), (16, 400), (1, 300)])
+def test_plain_instantiation_equals_general_path(pkg, dev, heads, batch):
+    """Causal 128-token sequences without a mask run the fused kernel's PLAIN
+    instantiation (mask bookkeeping compiled out). The same input with an
+    all-ones key bitmask runs the general instantiation; both must give
+    bit-identical outputs, in CTA-pair mode (few tiles) and one-CTA mode."""
+    import ctypes
+    kw = dict(batch_size=batch, seq_len=128, d_model=128, num_heads=heads, ffn_dim=128,
+              num_layers=2, causal=True)
+    _, cand = _pair(pkg, kw, 29, dev)
+    mdl = cand._prepare(dev)[3]
+    lib = pkg._lib.load()
+    x = torch.randn(batch, 128, 128, generator=torch.Generator().manual_seed(heads * batch)).to(dev)
+    bits = pkg.model.key_bitmask(torch.ones(batch, 128, dtype=torch.bool, device=dev))
+    y_plain = torch.empty_like(x)
+    y_general = torch.empty_like(x)
+    stream = torch.cuda.current_stream().cuda_stream
+    pkg._lib.check(lib.tfx_forward(ctypes.byref(mdl), x.data_ptr(), y_plain.data_ptr(), batch,
+                                   128, None, None, 0, stream), "tfx_forward")
+    pkg._lib.check(lib.tfx_forward_masked(ctypes.byref(mdl), x.data_ptr(), y_general.data_ptr(),
+                                          batch, 128, bits.data_ptr(), None, 0, stream),
+                   "tfx_forward_masked")
+    torch.cuda.synchronize()
+    assert torch.equal(y_plain, y_general)
