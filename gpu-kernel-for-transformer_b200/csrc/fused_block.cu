@@ -131,6 +131,16 @@ constexpr uint32_t kColX = 384;   // fp32 residual stream of the tile
 constexpr int kOffK2 = kOffW + 2 * kOpBytes;
 template <int HD>
 constexpr int weight_slots() { return HD == 8 ? 2 : kWSlots; }
+// One CTA per tile, head_dim >= 16: the QKV products run in the order Q, K,
+// V^T and Q is written into weight-ring slot 0, which holds Wq (every layer's
+// first weight lands in slot 0: six weights per layer, three slots) and is
+// released only after the layer's last score product. The Q and K epilogues
+// then overlap the later products, and the V^T epilogue the score products
+// (c2 3.279 -> 3.236 ms). CTA pairs (slower with it: c1 0.0488 -> 0.0515 ms)
+// and head_dim 8 (its second K copy takes the third slot) keep V^T, K, Q
+// with Q over h.
+template <int HD, bool SPLIT>
+constexpr bool q_first() { return HD >= 16 && !SPLIT; }
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 
@@ -481,7 +491,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* peer_free = peer_ctx + 1; // the peer's QKV products no longer read its sA
   // The next tile's fp32 input has landed in the sK/sV region (TMA).
   uint64_t* x_full = peer_free + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(x_full + 1);
+  // q_first: compute -> MMA: V^T in sV (after Q and K, which c2m reports).
+  uint64_t* c2m_vt = x_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(c2m_vt + 1);
   const uint32_t rank = SPLIT ? cluster_ctarank() : 0u;
   const uint32_t peer = rank ^ 1u;
   const int h0 = static_cast<int>(rank) * HL, h1 = h0 + HL;
@@ -505,6 +517,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(peer_ctx, kComputeWarps);
     mbar_init(peer_free, kComputeWarps);
     mbar_init(x_full, 1);
+    mbar_init(c2m_vt, kComputeWarps);
     fence_mbar_init();
   }
   grid_dep_wait();
@@ -558,7 +571,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < 6; ++c) {
           const CUtensorMap* m =
               c < 3 ? &p.w_qkv[l] : (c == 3 ? &p.w_out[l] : (c == 4 ? &p.w_in[l] : &p.w_fo[l]));
-          const int row0 = c < 3 ? kT * (2 - c) : 0;  // Wv, Wk, Wq
+          // Wq, Wk, Wv (q_first) or Wv, Wk, Wq, then Wo, W1, W2.
+          const int row0 = c < 3 ? kT * (q_first<HD, SPLIT>() ? c : 2 - c) : 0;
           if (!mbar_wait_sleep(&w_empty[slot], ph ^ 1, p.err, kDevTimeoutEmpty)) {
             ok = false;
             break;
@@ -589,6 +603,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t mph_o[2] = {0, 0};  // this thread's view of the O-buffer barriers
     uint32_t mph_p[2] = {0, 0};  // ... and of the P-ready barriers
     uint32_t ph_peer = 0;        // SPLIT: phase of peer_ctx
+    uint32_t c2m_vt_ph = 0;      // q_first: phase of c2m_vt
     auto wait_c2m = [&]() {
       const bool r = mbar_wait_sleep(c2m, c2m_ph, p.err, kDevTimeoutOther);
       c2m_ph ^= 1;
@@ -626,8 +641,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if constexpr (HD == 8)  // one K=16 step over the head pair; the K copy zeroes the other head
         mma_chain<1>(tmem + ((h & 1) ? kColS1 : kColS0), dA, 16 * (h >> 1), (h & 1) ? dK2 : dK,
                      16 * (h >> 1), id128);
-      else
-        mma_chain<HD / 16>(tmem + ((h & 1) ? kColS1 : kColS0), dA, h * HD, dK, h * HD, id128);
+      else  // Q in weight slot 0 (q_first) or over h in sA
+        mma_chain<HD / 16>(tmem + ((h & 1) ? kColS1 : kColS0), q_first<HD, SPLIT>() ? dW0 : dA,
+                           h * HD, dK, h * HD, id128);
       mma_commit(&m2c_s[h & 1]);
     };
     // A tile's fp32 input -> the 64 KB sK/sV region as four 32-column boxes
@@ -649,24 +665,52 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int l = 0; l < L && ok; ++l) {
         uint64_t w;
         if (!(ok = wait_c2m())) break;  // LN1 output in sA
-        // V^T, K, Q, each with its own commit: the compute warps store V^T
-        // and K while the later GEMMs run; Q comes last because it is
-        // written over h in sA, which all three read.
-        if (!(ok = take_w(w))) break;
-        mma_chain<kT / 16>(tmem + 256, w, 0, dA, 0, id128);  // V^T = Wv . h^T
-        release_w();
-        mma_commit(m2c_v);
-        if (!(ok = take_w(w))) break;
-        mma_chain<kT / 16>(tmem + 128, dA, 0, w, 0, id128);  // K
-        release_w();
-        mma_commit(m2c_k);
-        if (!(ok = take_w(w))) break;
-        mma_chain<kT / 16>(tmem + 0, dA, 0, w, 0, id128);  // Q
-        release_w();
-        mma_commit(m2c_g);
-        if (!(ok = wait_c2m())) break;  // Q, K, V^T in smem
-        issue_s(h0);
-        if (HL > 1) issue_s(h0 + 1);
+        if constexpr (q_first<HD, SPLIT>()) {
+          // Q (into slot 0's Wq, whose release waits for the last score
+          // product), K, V^T, each with its own commit.
+          if (!(ok = take_w(w))) break;
+          mma_chain<kT / 16>(tmem + 0, dA, 0, w, 0, id128);  // Q
+          if (++slot == WS) {  // slot 0 stays held: no w_empty commit yet
+            slot = 0;
+            ph ^= 1;
+          }
+          mma_commit(m2c_v);
+          if (!(ok = take_w(w))) break;
+          mma_chain<kT / 16>(tmem + 128, dA, 0, w, 0, id128);  // K
+          release_w();
+          mma_commit(m2c_k);
+          if (!(ok = take_w(w))) break;
+          mma_chain<kT / 16>(tmem + 256, w, 0, dA, 0, id128);  // V^T = Wv . h^T
+          release_w();
+          mma_commit(m2c_g);
+          if (!(ok = wait_c2m())) break;  // Q (in slot 0) and K in smem
+          issue_s(h0);
+          if (HL > 1) issue_s(h0 + 1);
+          if (h0 + 2 >= h1) mma_commit(&w_empty[0]);  // no later score product reads Q
+          // V^T in sV (its accumulator columns become the O buffers).
+          if (!(ok = mbar_wait_sleep(c2m_vt, c2m_vt_ph, p.err, kDevTimeoutOther))) break;
+          c2m_vt_ph ^= 1;
+          tc_fence_after();
+        } else {
+          // V^T, K, Q, each with its own commit: the compute warps store V^T
+          // and K while the later GEMMs run; Q comes last because it is
+          // written over h in sA, which all three read.
+          if (!(ok = take_w(w))) break;
+          mma_chain<kT / 16>(tmem + 256, w, 0, dA, 0, id128);  // V^T = Wv . h^T
+          release_w();
+          mma_commit(m2c_v);
+          if (!(ok = take_w(w))) break;
+          mma_chain<kT / 16>(tmem + 128, dA, 0, w, 0, id128);  // K
+          release_w();
+          mma_commit(m2c_k);
+          if (!(ok = take_w(w))) break;
+          mma_chain<kT / 16>(tmem + 0, dA, 0, w, 0, id128);  // Q
+          release_w();
+          mma_commit(m2c_g);
+          if (!(ok = wait_c2m())) break;  // Q, K, V^T in smem
+          issue_s(h0);
+          if (HL > 1) issue_s(h0 + 1);
+        }
         for (int h = h0; h < h1 && ok; ++h) {
           // P_h written over S buffer h % 2 by all compute warps.
           if (!(ok = mbar_wait_sleep(&c2m_p[h & 1], mph_p[h & 1], p.err, kDevTimeoutOther))) break;
@@ -688,6 +732,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!(ok = mbar_wait_sleep(&m2c_o[h & 1], mph_o[h & 1], p.err, kDevTimeoutOther))) break;
             tc_fence_after();
             issue_s(h + 2);
+            if (q_first<HD, SPLIT>() && h + 2 == h1 - 1) mma_commit(&w_empty[0]);  // the last reader of Q
           }
           mph_o[h & 1] ^= 1;
         }
@@ -736,13 +781,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     // smem: the phase wrote an MMA operand to shared memory (generic-proxy
     // stores the tensor core must see); TMEM-only phases skip that fence.
-    auto signal = [&](bool smem = true) {
+    auto signal_to = [&](uint64_t* bar, bool smem) {
       tmem_st_wait();
       if (smem) fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(c2m);
+      if (lane == 0) mbar_arrive(bar);
     };
+    auto signal = [&](bool smem = true) { signal_to(c2m, smem); };
     const int S = PLAIN ? kT : p.seq;
     // Per head parity (odd heads: reversed rows): the query token of this
     // lane's S row, its key range (own sequence; causal) and the
@@ -862,14 +908,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int l = 0; l < L; ++l) {
         const float* lp = par + l * kParFloats;
         signal();  // LN1 output in sA
-        // QKV epilogue in the order the GEMMs complete, each split between the
-        // two warps of a lane quarter: V^T (half 0 takes the first half of the
-        // tokens of V^T row r, half 1 the second; V^T lanes are features), K,
-        // then Q (columns [64*half, +64), or with SPLIT 32 columns each of the
-        // CTA's 64-column block). After the last product only one TMEM round
-        // trip per warp is left.
-        if (!(ok = wait(m2c_v, kPhV))) break;
-        {
+        // QKV epilogues, each split between the two warps of a lane quarter:
+        // V^T (half 0 takes the first half of the tokens of V^T row r, half 1
+        // the second; V^T lanes are features), K and Q (columns [64*half,
+        // +64), or with SPLIT 32 columns each of the CTA's 64-column block).
+        auto vt_epilogue = [&]() {
           const float bv = lp[kPQkv + 256 + r];  // V bias of feature r
           const uint64_t bv2 = f2_pack(bv, bv);
           uint32_t ra[32], rb[32];
@@ -887,11 +930,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             f2_unpack(f2_add(f2_pack(__uint_as_float(rb[j]), __uint_as_float(rb[j + 1])), bv2),
                       v[j], v[j + 1]);
           store_row<4>(sV, r, 64 * half + 32, v);
-        }
-        // 32-column chunks c0 .. c0+NC-1 of Q (TMEM/bias chunk q0 = 0) or K (4).
+        };
+        // 32-column chunks c0 .. c0+NC-1 of Q (TMEM/bias chunk q0 = 0, stored
+        // at q_dst) or K (4).
         constexpr int NC = SPLIT ? 1 : 2;
         const int c0 = SPLIT ? 2 * static_cast<int>(rank) + half : 2 * half;
-        auto qk_epilogue = [&](int q0) {
+        auto qk_epilogue = [&](int q0, uint32_t q_dst) {
           uint32_t ra[NC][32];
 #pragma unroll
           for (int n = 0; n < NC; ++n) tmem_ld32(tl + 32 * (q0 + c0 + n), ra[n]);
@@ -903,19 +947,32 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(ra[n][j]);
             add_bias32(v, lp + kPQkv + 32 * (q0 + c0 + n));
             if (q0 == 0)
-              store_q32<HD>(sA, r, 32 * (c0 + n), v);
+              store_q32<HD>(q_dst, r, 32 * (c0 + n), v);
             else if constexpr (HD == 8)
               store_k_split(sK, sbase + kOffK2, r, 32 * (c0 + n), v);
             else
               store_row<4>(sK, r, 32 * (c0 + n), v);
           }
         };
-        if (!(ok = wait(m2c_k, kPhK))) break;
-        qk_epilogue(4);
-        // Q goes over h in sA, which all three products read: after the last.
-        if (!(ok = wait(m2c_g, kPhG))) break;
-        qk_epilogue(0);
-        signal();
+        if constexpr (q_first<HD, SPLIT>()) {
+          if (!(ok = wait(m2c_v, kPhV))) break;  // Q product complete: Wq's slot is free
+          qk_epilogue(0, sbase + kOffW);        // Q into weight slot 0
+          if (!(ok = wait(m2c_k, kPhK))) break;
+          qk_epilogue(4, 0u);
+          signal();  // Q and K in smem: the score products may start
+          if (!(ok = wait(m2c_g, kPhG))) break;  // V^T product complete (the last reader of h)
+          vt_epilogue();
+          signal_to(c2m_vt, true);
+        } else {
+          if (!(ok = wait(m2c_v, kPhV))) break;
+          vt_epilogue();
+          if (!(ok = wait(m2c_k, kPhK))) break;
+          qk_epilogue(4, 0u);
+          // Q goes over h in sA, which all three products read: after the last.
+          if (!(ok = wait(m2c_g, kPhG))) break;
+          qk_epilogue(0, sA);
+          signal();
+        }
         if constexpr (SPLIT) {
           // This CTA's QKV products are complete (m2c_g): the block of sA the
           // peer's heads own may now take the peer's ctx.
