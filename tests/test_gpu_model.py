@@ -131,6 +131,7 @@ FUSED_CASES = [
     (3, 128, 128, 2, 128, 2, True),     # head_dim 64
     (2, 128, 128, 1, 128, 2, True),     # head_dim 128
     (5, 32, 128, 4, 128, 2, True),      # 4 sequences per tile, partial last tile
+    (1203, 32, 128, 4, 128, 2, True),   # one CTA per tile (301 tiles), partial last tile
     (7, 1, 128, 4, 128, 2, True),       # one token per sequence
     (6, 64, 128, 4, 128, 2, False),     # non-causal, block-diagonal tiles
     (2, 16, 128, 4, 128, 3, True),
