@@ -199,7 +199,9 @@ typedef struct tfx_model {
 TFX_API int64_t tfx_forward_workspace_bytes(const tfx_model* model, int batch, int seq);
 
 /*
- * Whole forward: y = final_norm(blocks(x)), x and y [batch, seq, D] fp32
+ * Whole forward: y = final_norm(blocks(x)), x and y [batch, seq, D] fp32,
+ * 16-byte aligned (TFX_ERR_MISALIGNED otherwise; the fused kernel reads x
+ * with TMA), batch * seq below 2^31 tokens
  * (the two ranges must not overlap: TFX_ERR_INVALID_ARGUMENT). valid_len: NULL or [batch] int32 prefix lengths
  * (padded rows of y are zeroed, padded keys masked). workspace: device
  * buffer of at least tfx_forward_workspace_bytes() (may be NULL when that
