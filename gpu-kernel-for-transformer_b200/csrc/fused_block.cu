@@ -14,8 +14,9 @@
 // last layer runs its out-projection and FFN.
 //
 // Roles (320 threads):
-//   warp 0      TMA producer: per layer Wv, Wk, Wq, Wo, W1, W2 (128x128 fp16
-//               each, 128-byte swizzle) into a 3-slot ring
+//   warp 0      TMA producer: per layer Wq, Wk, Wv (q_first) or Wv, Wk, Wq,
+//               then Wo, W1, W2 (128x128 fp16 each, 128-byte swizzle) into a
+//               3-slot ring
 //   warp 1      TMEM owner (all 512 columns) + single-thread tcgen05.mma issuer
 //   warps 2..9  compute, two warps per TMEM lane quarter: lane l of warp w
 //               owns row 32*(w%4)+l of every 128-row accumulator and HALF of
@@ -35,11 +36,15 @@
 //      operand of P.V), K = h.Wk^T, Q = h.Wq^T, each committed on its own
 //   c: + biases -> V^T into sV, K into sK (while the next GEMM runs), Q into
 //      sA last (over h, which all three GEMMs read)
+//      (q_first, one CTA per tile and head_dim >= 16: Q, K, V^T instead, Q
+//      into the weight slot Wq came from; the S products start after the Q
+//      and K epilogues, P.V after the V^T epilogue)
 //   m: S_0 -> S buffer 0, S_1 -> S buffer 1
 //   per head h (b = h % 2):
 //     c: softmax row of S_h -> P_h (fp16, <= 1) written over its own S buffer
 //     m: O_h = P_h . V_h -> O buffer b ; S_{h+2} -> S buffer b
-//     c: (while the MMAs run) ctx_{h-1} = O_{h-1} / l_{h-1} -> sA over Q_{h-1}
+//     c: (while the MMAs run) ctx_{h-1} = O_{h-1} / l_{h-1} -> sA (over Q_{h-1},
+//        or over h with q_first)
 //   m: x += ctx . Wo^T         c: LN2(x) -> TMEM A operand; x + b2 -> TMEM x
 //   m: acc = h2 . W1^T         c: g = gelu(acc + b1) -> TMEM A operand
 //   m: x += g . W2^T           c: next LN1 (x + next bo -> TMEM x) or final LN -> y
