@@ -132,6 +132,10 @@ FUSED_CASES = [
     (2, 128, 128, 1, 128, 2, True),     # head_dim 128
     (5, 32, 128, 4, 128, 2, True),      # 4 sequences per tile, partial last tile
     (1203, 32, 128, 4, 128, 2, True),   # one CTA per tile (301 tiles), partial last tile
+    # One CTA per tile (more tiles than half the SMs): the Q, K, V^T product order
+    (160, 128, 128, 8, 128, 2, True),   # head_dim 16
+    (160, 128, 128, 2, 128, 2, True),   # head_dim 64
+    (160, 128, 128, 4, 128, 2, True, 0.5),  # head_dim 32, prefix padding (general instantiation)
     (7, 1, 128, 4, 128, 2, True),       # one token per sequence
     (6, 64, 128, 4, 128, 2, False),     # non-causal, block-diagonal tiles
     (2, 16, 128, 4, 128, 3, True),
